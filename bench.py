@@ -1,0 +1,429 @@
+"""Benchmark: packed GEMV HBM GB/s (M=1) and packed GEMM TFLOP/s (M=4096) on B200.
+
+Default workload (one "step"): BASELINE config 2 at M=1 -- y[1, 8192] = x[1, 8192] @ W^T with
+W an FP4 E2M1 (8192, 8192) packed matrix with per-32 E8M0 scales, bf16 x and y. Each step
+reads a different one of C resident weight copies (C * 35.7 MB > 4 x 126 MB L2), so every
+step streams its weights from HBM. The timed region replays a CUDA graph of exactly K
+packed-GEMV launches. A secondary measurement (key "gemm") times BASELINE config 3
+(FP6 E3M2, M=4096, K=4096, N=14336, per-row fp16 scales) in TFLOP/s.
+
+Multi-GPU (torchrun, one process per GPU): every rank runs the same per-GPU workload on its
+own weights (independent matrices, no collective in the data path) -> "scaling": "weak";
+value = total bytes of all ranks / max-over-ranks time.
+
+``--impl reference`` times the CPU restatement of the reference's path (the reference
+itself is tinygrad-on-DX12 Python and cannot run here) on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+L2_BYTES = 126 * 2**20
+GEMV_CFG = dict(fmt="fp4_e2m1", n=8192, k=8192, block=32, scale="e8m0", xdt="bfloat16", m=1)
+GEMM_CFG = dict(fmt="fp6_e3m2", n=14336, k=4096, block=4096, scale="f16row", xdt="float16", m=4096)
+
+
+def algo_bytes(cfg) -> int:
+    """Algorithmic bytes per call: packed W + scales + x + y (SURVEY 8(d) figures)."""
+    n, k, m = cfg["n"], cfg["k"], cfg["m"]
+    bits = 6 if cfg["fmt"].startswith("fp6") else 4
+    w = n * k * bits // 8
+    nblk = -(-k // cfg["block"])
+    sbytes = n * nblk * (1 if cfg["scale"] == "e8m0" else 2)
+    xb = m * k * 2
+    yb = m * n * 2
+    return w + sbytes + xb + yb
+
+
+def algo_flops(cfg) -> int:
+    return 2 * cfg["m"] * cfg["n"] * cfg["k"]
+
+
+# ------------------------------------------------------------------------------------
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in pathlib.Path(self.file.name).read_text().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        finally:
+            os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for nm, val in zip(names, r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------------------------
+def make_weights(cfg, device, copies: int, seed: int):
+    """Random packed weights resident on the device (codes uniform over the format's payloads)."""
+    import torch
+    import tinygrad_dx12_b200 as tg
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    n, k = cfg["n"], cfg["k"]
+    bits = 6 if cfg["fmt"].startswith("fp6") else 4
+    nbytes = n * k * bits // 8
+    ws = []
+    for _ in range(copies):
+        data = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device=device, generator=g)
+        if cfg["scale"] == "e8m0":
+            e = torch.randint(-8, -1, (n, k // cfg["block"]), device=device, generator=g)
+            scales = (e + 127).to(torch.uint8).view(torch.float8_e8m0fnu)
+            ws.append(tg.PackedTensor(data, cfg["fmt"], (n, k), scales, cfg["block"]))
+        else:
+            s = torch.rand((n, 1), device=device, generator=g) * 0.04 + 0.01
+            ws.append(tg.PackedTensor(data, cfg["fmt"], (n, k), s.to(torch.float16), k))
+    return ws
+
+
+def run_gpu_arm(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+    import tinygrad_dx12_b200 as tg
+    from tinygrad_dx12_b200 import _lib
+    from tinygrad_dx12_b200.linalg import _packed_linear, linear_plan
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device, timeout=__import__("datetime").timedelta(seconds=120))
+    cfg = dict(GEMV_CFG)
+    xdt = getattr(torch, cfg["xdt"])
+    per_copy = cfg["n"] * cfg["k"] // 2
+    copies = max(4, -(-4 * L2_BYTES // per_copy))
+    ws = make_weights(cfg, device, copies, seed=1234 + rank)
+    x = torch.randn((cfg["m"], cfg["k"]), device=device).to(xdt)
+    y = torch.empty((cfg["m"], cfg["n"]), device=device, dtype=xdt)
+    plan = linear_plan(ws[0], xdt, cfg["m"], xdt)
+    descs = [w.desc() for w in ws]
+    fn = _lib.lib().b200_packed_linear
+    xdt_code, ydt_code = _lib.DT[cfg["xdt"]], _lib.DT[cfg["xdt"]]
+
+    def launch(i, stream):
+        rc = fn(ctypes.byref(descs[i % copies]), x.data_ptr(), xdt_code, cfg["m"], cfg["k"], 1, y.data_ptr(),
+                ydt_code, cfg["n"], 1, 0, stream)
+        if rc:
+            raise RuntimeError(_lib.last_error())
+
+    # warm-up (untimed) through plain launches, then capture exactly K launches in a graph
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            launch(i, stream.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(args.steps):
+            launch(args.warmup + i, stream.cuda_stream)
+    graph.replay()  # one untimed replay (graph upload)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        ev0.record(stream)
+        graph.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    bytes_step = algo_bytes(cfg)
+    per_launch_s = ms / 1e3 / args.steps
+    value = bytes_step * args.steps * world / (ms_max / 1e3) / 1e9
+
+    # e2e through the public API: H2D x from pinned memory, matmul, D2H y, every step
+    xh = torch.randn((cfg["m"], cfg["k"])).to(xdt).pin_memory()
+    yh = torch.empty((cfg["m"], cfg["n"]), dtype=xdt).pin_memory()
+    for i in range(3):
+        xd = xh.to(device, non_blocking=True)
+        yh.copy_(tg.matmul(ws[i % copies], xd.t(), dtype=xdt).t(), non_blocking=True)
+    torch.cuda.synchronize()
+    e_steps = max(10, min(args.steps, 200))
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e_steps):
+        xd = xh.to(device, non_blocking=True)
+        yh.copy_(tg.matmul(ws[i % copies], xd.t(), dtype=xdt).t(), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    ems = torch.tensor([e0.elapsed_time(e1)], device=device)
+    if world > 1:
+        dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+    e2e_value = bytes_step * e_steps * world / (float(ems.item()) / 1e3) / 1e9
+
+    gemm = None
+    if not args.no_gemm:
+        gemm = run_gemm(args, device, world, rank)
+    peaks = measured_peaks()
+    result = None
+    if rank == 0:
+        achieved = bytes_step / per_launch_s / 1e9
+        result = {
+            "metric": "packed GEMV HBM GB/s (M=1)",
+            "value": round(value, 1),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_max / args.steps, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "fp4_e2m1 x bf16 -> fp32 acc",
+            "data": "synthetic (seeded random codes / E8M0 scales / N(0,1) bf16 x), random-init weights",
+            "config": {"workload": "c2 FP4 E2M1 packed GEMV M=1, N=K=8192, per-32 E8M0 scales, bf16 x/y",
+                       "m": cfg["m"], "n": cfg["n"], "k": cfg["k"], "kernel": plan,
+                       "weight_copies": copies, "l2": "inputs larger than L2: rotating %d weight copies (%.0f MB)" % (
+                           copies, copies * bytes_step / 1e6),
+                       "timing": "CUDA graph of K launches, CUDA events on the launch stream",
+                       "parallelism": f"independent weights per GPU x{world}"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                         "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)",
+                         "algorithmic_bytes_per_launch": bytes_step},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": cfg["m"] * cfg["k"] * 2, "d2h_bytes_per_step": cfg["m"] * cfg["n"] * 2,
+                    "path": "tinygrad_dx12_b200.matmul(W, x.T, dtype=bf16) with pinned-host x in and y out"},
+            "gpu_launches": args.steps,
+            "clocks": clk.summary(),
+        }
+        if gemm is not None:
+            result["gemm"] = gemm
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def run_gemm(args, device, world, rank):
+    import torch
+    import torch.distributed as dist
+    from tinygrad_dx12_b200 import _lib
+    from tinygrad_dx12_b200.linalg import linear_plan
+
+    cfg = dict(GEMM_CFG)
+    xdt = torch.float16
+    w = make_weights(cfg, device, 1, seed=99 + rank)[0]
+    x = (torch.randn((cfg["m"], cfg["k"]), device=device) / 8).to(xdt)
+    y = torch.empty((cfg["m"], cfg["n"]), device=device, dtype=xdt)
+    plan = linear_plan(w, xdt, cfg["m"], xdt)
+    d = w.desc()
+    fn = _lib.lib().b200_packed_linear
+    stream = torch.cuda.Stream(device)
+
+    def launch():
+        rc = fn(ctypes.byref(d), x.data_ptr(), _lib.DT["float16"], cfg["m"], cfg["k"], 1, y.data_ptr(),
+                _lib.DT["float16"], cfg["n"], 1, 0, stream.cuda_stream)
+        if rc:
+            raise RuntimeError(_lib.last_error())
+
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=device)
+    steps = max(3, min(args.steps, 20))
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            launch()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        with torch.cuda.stream(stream):
+            flush.fill_(1)  # L2 flush between timed launches
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        launch()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = statistics.median(times)
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    flops = algo_flops(cfg)
+    tflops = flops / (ms / 1e3) / 1e12
+    peaks = measured_peaks()
+    return {
+        "metric": "packed GEMM TFLOP/s (M=4096)",
+        "value": round(tflops * world, 2),
+        "unit": "TFLOP/s",
+        "ms_per_call": round(ms, 4),
+        "config": {"workload": "c3 FP6 E3M2 packed GEMM M=4096 K=4096 N=14336, per-row fp16 scales, fp16 x/y",
+                   "kernel": plan, "l2": "flushed (256 MB write) before each timed launch", "timed_launches": steps},
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(tflops / peaks["bf16_tflops"], 4), "traffic": None,
+                     "peak_source": peaks["source"] + " (MEASURED_PEAKS.json bf16_tflops, dense fp16/bf16 kind)",
+                     "algorithmic_flops_per_launch": flops},
+    }
+
+
+# ------------------------------------------------------------------------------------
+def cpu_port_run(cfg, nthreads: int, budget_s: float, seed: int = 0):
+    """Time the oracle's C restatement of the reference path on this host's cores."""
+    from oracle import build as obuild
+    from oracle import packed_ref as ref
+
+    clib = obuild.load()
+    rng = np.random.default_rng(seed)
+    spec = ref.make_packed(rng, cfg["fmt"], cfg["n"], cfg["k"], cfg["block"], cfg["scale"])
+    sc = ref.e8m0_bytes(spec.scales) if cfg["scale"] == "e8m0" else spec.scales
+    sdt = 16 if cfg["scale"] == "e8m0" else 12
+    x = rng.standard_normal((cfg["m"], cfg["k"])).astype(np.float32)
+    xs = x.astype(ref.BF16) if cfg["xdt"] == "bfloat16" else x.astype(np.float16)
+    xdt = 13 if cfg["xdt"] == "bfloat16" else 12
+    y = np.empty((cfg["m"], cfg["n"]), np.float32)
+    P = ctypes.c_void_p
+
+    def once():
+        rc = clib.oref_linear(spec.data.ctypes.data_as(P), spec.data.size, {"int4": 0, "uint4": 1, "fp4_e2m1": 2,
+                              "fp6_e2m3": 3, "fp6_e3m2": 4}[cfg["fmt"]], cfg["n"], cfg["k"], sc.ctypes.data_as(P), sdt,
+                              spec.block_size, np.ascontiguousarray(xs).ctypes.data_as(P), xdt, cfg["m"],
+                              y.ctypes.data_as(P), nthreads)
+        assert rc == 0
+
+    once()  # warm-up
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        once()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start >= budget_s and len(times) >= 3:
+            break
+    return statistics.median(times), len(times)
+
+
+def cpu_baseline(nthreads: int, budget_s: float) -> dict:
+    cfg = dict(GEMV_CFG)
+    sec, reps = cpu_port_run(cfg, nthreads, budget_s)
+    return {"value": round(algo_bytes(cfg) / sec / 1e9, 3), "unit": "GB/s", "cores": nthreads, "kind": "port",
+            "sample": f"{reps} full c2 M=1 calls (8192x8192 FP4, E8M0 scales, bf16 x), median "
+                      f"{sec * 1e3:.1f} ms/call; oracle/cpu_ref.c decode-to-fp32 row + fp32 dot, OpenMP"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-gemm", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world, rank, local = dist_env()
+    nthreads = os.cpu_count() or 1
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cfg = dict(GEMV_CFG)
+        per_step = []
+        for _ in range(args.warmup):
+            cpu_port_run(cfg, nthreads, 0.0)
+        for _ in range(args.steps):
+            sec, _ = cpu_port_run(cfg, nthreads, 0.0)
+            per_step.append(sec)
+        tot = sum(per_step)
+        value = algo_bytes(cfg) * args.steps / tot / 1e9
+        print(json.dumps({
+            "impl": "reference", "metric": "packed GEMV HBM GB/s (M=1)", "value": round(value, 3), "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(tot / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp4_e2m1 x bf16 -> fp32 acc", "data": "synthetic",
+            "config": {"workload": "c2 FP4 E2M1 packed GEMV M=1, N=K=8192, per-32 E8M0 scales, bf16 x/y",
+                       "note": "the reference runs this path through tinygrad's CPU device; tinygrad is not "
+                               "installable here (no network, Python 3.14 syntax), so the timed code is the CPU "
+                               "restatement oracle/cpu_ref.c of the same arithmetic"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": nthreads, "kind": "port",
+                             "sample": f"{args.steps} full c2 M=1 calls"},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }))
+        return
+
+    res = run_gpu_arm(args, world, rank, local)
+    if rank == 0 and res is not None:
+        if not args.no_cpu and world == 1:
+            res["cpu_baseline"] = cpu_baseline(nthreads, args.cpu_budget)
+        print(json.dumps(res))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,134 @@
+"""Fused packed linear (GEMV / tcgen05 GEMM / SIMT) against the float32 oracle.
+
+Shapes cover BASELINE.json's configs (c1 and c2 at full size; c3 at full K with fewer rows,
+plus a sampled-rows check at full size), odd tails, every format and scale dtype, and the
+three x / y dtypes. Tolerances: tests/helpers.py.
+"""
+
+import functools
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import packed_ref as ref
+from tests.helpers import TORCH_OF, assert_close, oracle_scales, to_device
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@functools.lru_cache(maxsize=8)
+def _spec(fmt, rows, cols, bs, kind, seed):
+    return ref.make_packed(np.random.default_rng(seed), fmt, rows, cols, bs, kind)
+
+
+_WCACHE: dict = {}
+
+
+def _wref(spec, scale_dtype):
+    key = (id(spec), scale_dtype)
+    if key not in _WCACHE:
+        if len(_WCACHE) > 4:
+            _WCACHE.clear()
+        sc, sdt = oracle_scales(spec, scale_dtype)
+        _WCACHE[key] = ref.dequant(spec.data, spec.format, spec.shape, sc, spec.block_size, "float32", sdt)
+    return _WCACHE[key]
+
+
+def _run(spec, scale_dtype, m, xdt, ydt, path="auto", seed=0, xscale=1.0):
+    import tinygrad_dx12_b200 as tg
+    from tinygrad_dx12_b200.linalg import _packed_linear, linear_plan
+
+    rng = np.random.default_rng(seed)
+    w = to_device(spec, DEV, scale_dtype)
+    x = torch.from_numpy((rng.standard_normal((m, spec.shape[1])) * xscale).astype(np.float32)).to(DEV).to(TORCH_OF[xdt])
+    plan = linear_plan(w, x.dtype, m, TORCH_OF[ydt], path)
+    if plan is None:
+        pytest.skip(f"path {path} does not take fmt={spec.format} scale={scale_dtype} m={m} x={xdt}")
+    y = _packed_linear(w, x, TORCH_OF[ydt], path).float().cpu().numpy()
+    r = x.float().cpu().numpy() @ _wref(spec, scale_dtype).T
+    assert_close(y, r, ydt)
+    return plan, x, w, y
+
+
+PATHS = ["auto", "gemv", "simt", "gemm"]
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 17, 32])
+def test_c1_int4_gemv(path, m):
+    """BASELINE config 1 shape: INT4 4096x4096, per-32 fp16 scales, fp16 x and y."""
+    spec = _spec("int4", 4096, 4096, 32, "f16u", 1)
+    _run(spec, None, m, "float16", "float16", path)
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("m", [1, 8, 32])
+@pytest.mark.parametrize("scale", ["e8m0", "bfloat16"])
+def test_c2_fp4_gemv(path, m, scale):
+    """FP4 E2M1 8192x8192, per-32 2^e scales (E8M0 bytes or decoded bf16), bf16 x/y."""
+    spec = _spec("fp4_e2m1", 8192, 8192, 32, "e8m0", 2)
+    _run(spec, scale, m, "bfloat16", "bfloat16", path)
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("m", [64, 256, 300])
+def test_c3_fp6_gemm_reduced(path, m):
+    """BASELINE config 3 at full K=4096 with 1024 rows: FP6 E3M2, per-row fp16 scales, fp16 x (N(0,1)/8)."""
+    spec = _spec("fp6_e3m2", 1024, 4096, 4096, "f16row", 3)
+    _run(spec, None, m, "float16", "float16", path, xscale=0.125)
+
+
+@pytest.mark.parametrize("fmt", list(ref.FORMATS))
+@pytest.mark.parametrize("scale", [None, "float16", "bfloat16", "float32", "e8m0"])
+@pytest.mark.parametrize("xdt", ["float16", "bfloat16", "float32"])
+@pytest.mark.parametrize("m", [1, 5, 33, 130])
+def test_formats_scales_dtypes(fmt, scale, xdt, m):
+    rng = np.random.default_rng(7)
+    kind = None if scale is None else ("e8m0" if scale == "e8m0" else "f16u")
+    spec = ref.make_packed(rng, fmt, 384, 512, 64, kind)
+    if scale not in (None, "e8m0"):
+        spec = ref.PackedSpec(spec.data, fmt, spec.shape, spec.scales.astype(ref.np_dtype(scale)), 64)
+    _run(spec, scale, m, xdt, "float32", "auto")
+
+
+@pytest.mark.parametrize("rows,cols,m", [(1, 32, 1), (3, 64, 2), (129, 96, 7), (1000, 160, 33), (17, 4096, 1)])
+@pytest.mark.parametrize("fmt", ["int4", "fp6_e2m3"])
+def test_odd_shapes(rows, cols, m, fmt):
+    spec = ref.make_packed(np.random.default_rng(rows), fmt, rows, cols, 32, "f16u")
+    _run(spec, None, m, "float16", "float32", "auto")
+
+
+@pytest.mark.parametrize("ydt", ["float16", "bfloat16", "float32"])
+def test_output_dtypes(ydt):
+    spec = ref.make_packed(np.random.default_rng(11), "fp4_e2m1", 512, 1024, 32, "e8m0")
+    _run(spec, "e8m0", 4, "bfloat16", ydt)
+
+
+def test_public_api_call_forms():
+    """matmul(W, x.T).T and matvec(W, v) give the same numbers as the fused call."""
+    import tinygrad_dx12_b200 as tg
+
+    spec = ref.make_packed(np.random.default_rng(5), "int4", 256, 512, 32, "f16u")
+    w = to_device(spec, DEV)
+    x = torch.randn(3, 512, device=DEV, dtype=torch.float16)
+    y = tg.matmul(w, x.t())
+    assert y.shape == (256, 3) and y.dtype == torch.float32
+    r = ref.packed_linear_ref(spec, x.float().cpu().numpy())
+    assert_close(y.t().cpu().numpy(), r, "float32")
+    v = tg.matvec(w, x[0])
+    assert v.shape == (256,) and v.dtype == torch.float32
+    assert_close(v.cpu().numpy()[None], r[:1], "float32")
+    v16 = tg.matvec(w, x[0], torch.float16)
+    assert v16.dtype == torch.float16
+    vt = tg.matvec(w, x[0], thread=True)
+    assert_close(vt.cpu().numpy()[None], r[:1], "float32")
+    vf = tg.matvec(w, x[0], thread=False)
+    assert_close(vf.cpu().numpy()[None], r[:1], "float32")
+    yt = tg.matmul(w, x.t(), scope="tiled")
+    assert_close(yt.t().cpu().numpy(), r, "float32")
+    # a non-transposed (K, M) right operand is staged and gives the same result
+    yc = tg.matmul(w, x.t().contiguous(), dtype=torch.float16)
+    assert yc.dtype == torch.float16
+    assert_close(yc.t().float().cpu().numpy(), r, "float16")

@@ -1,0 +1,14 @@
+"""B200 (sm_100a) backend for tinygrad-dx12's packed low-bit matmul path.
+
+Importing the package registers the backend without opening hardware, as
+``import tinygrad_dx12`` does (tinygrad-dx12 ``src/tinygrad_dx12/__init__.py:8-10``).
+"""
+
+from .compat import register as register
+from .packed import FORMATS, FP8_CANDIDATES, PackedTensor, matrix_intermediate
+from .linalg import choose_matrix, matmul, matvec
+
+register()
+
+__all__ = ["register", "FORMATS", "FP8_CANDIDATES", "PackedTensor", "matrix_intermediate", "matmul", "matvec",
+           "choose_matrix"]

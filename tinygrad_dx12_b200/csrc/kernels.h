@@ -1,0 +1,46 @@
+// kernels.h -- host-side launchers shared between the C-ABI (capi.cu) and kernel files.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/b200_packed.h"
+
+namespace b200 {
+
+// Arguments of a fused packed linear y[m, n] = sum_k x[m, k] * W[n, k].
+struct LinearArgs {
+  const uint8_t *w;  // packed bytes
+  const void *scales;
+  int fmt, sdt;
+  int64_t rows, cols, block, nblk;
+  const void *x;
+  int xdt;
+  int64_t m, ldx;  // x row stride in elements (k stride is 1)
+  void *y;
+  int ydt;
+  int64_t ldy_m, ldy_n;
+};
+
+int32_t launch_dequant(const b200_packed_desc *w, int64_t begin, int64_t count, void *out, int32_t out_dtype,
+                       bool fp8_exact, cudaStream_t stream);
+
+// fp32 CUDA-core fused kernel (any M; x f16/bf16/f32).
+bool simt_supported(const LinearArgs &a);
+int32_t launch_gemv_simt(const LinearArgs &a, cudaStream_t stream);
+
+// tensor-core decode GEMV (M <= 32; x f16/bf16).
+bool gemv_tc_supported(const LinearArgs &a);
+int32_t launch_gemv_tc(const LinearArgs &a, cudaStream_t stream);
+
+// tcgen05 GEMM (M > 32; x f16/bf16).
+bool gemm_supported(const LinearArgs &a);
+int32_t launch_gemm(const LinearArgs &a, cudaStream_t stream);
+
+int32_t launch_matmul_generic(const void *a, int adt, int64_t sam, int64_t sak, const void *b, int bdt, int64_t sbk,
+                              int64_t sbn, void *c, int cdt, int64_t scm, int64_t scn, int64_t M, int64_t N, int64_t K,
+                              int accdt, cudaStream_t stream);
+int32_t launch_cast(const void *src, int sdt, void *dst, int ddt, int64_t n, cudaStream_t stream);
+int32_t launch_wait_flag(const int32_t *flag, int32_t expect, int64_t max_spins, int32_t *status, cudaStream_t stream);
+
+}  // namespace b200

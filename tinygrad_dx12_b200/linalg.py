@@ -1,0 +1,191 @@
+"""Public matrix API on the B200 device: ``matmul`` and ``matvec``.
+
+Drop-in for tinygrad-dx12 ``src/tinygrad_dx12/codegen/linalg.py`` with the same signatures,
+argument checks and dtype rules:
+
+* ``matmul(a, b, scope="auto", tile=None, dtype=None)`` (linalg.py:136-223). ``dtype`` sets
+  the output precision; every fused kernel accumulates in float32 (the reference leaves
+  internal arithmetic to the device, linalg.py:152-155).
+* ``matvec(matrix, vector, output_dtype=None, thread=None)`` (linalg.py:226-298).
+* ``choose_matrix`` (linalg.py:90-133) reports the kernel the library selects.
+
+Scopes. ``auto`` selects a fused kernel when one supports the operands and otherwise the
+ordinary path (decode kernel + the library's generic matmul kernel), like the reference's
+fallback to ordinary compute. ``Wave`` requests the warp-scope fused decode GEMV,
+``ThreadGroup`` the CTA-scope tcgen05 GEMM; when the library rejects an explicit scope a
+``RuntimeError`` is raised. ``tiled`` is ordinary compute. Unknown scopes raise ``ValueError``.
+
+The fused call form is ``matmul(W, x.T)`` with ``W`` a ``PackedTensor`` of shape (N, K) and
+``x`` (M, K): the result is (N, M) (a transposed view of a row-major (M, N) buffer), so
+``matmul(W, x.T).T`` is ``x @ W^T``. No path runs on the CPU.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from . import dtypes as D
+from .packed import PackedTensor, matrix_intermediate, stream_ptr, ctypes_ref
+
+SCOPES = ("auto", "Wave", "ThreadGroup", "tiled")
+FUSED_IO = (torch.float16, torch.bfloat16, torch.float32)
+_SCOPE_PATHS = {"auto": ("auto",), "Wave": ("gemv", "simt"), "ThreadGroup": ("gemm",)}
+
+
+def _device_of(op) -> torch.device:
+    return op.data.device if isinstance(op, PackedTensor) else op.device
+
+
+def _check_cuda(device: torch.device) -> None:
+    if device.type != "cuda":
+        raise ValueError(f"the B200 matrix API requires CUDA tensors (got device {device})")
+
+
+def _generic_matmul(lhs: torch.Tensor, rhs: torch.Tensor, out_dtype: torch.dtype, acc_dtype: torch.dtype) -> torch.Tensor:
+    """Ordinary matmul through ``b200_matmul_generic`` (linalg.py:188-189, the 'tiled' scope)."""
+    m, k = lhs.shape
+    n = rhs.shape[1]
+    fp8_out = out_dtype in (torch.float8_e4m3fn, torch.float8_e5m2)
+    out = torch.empty((m, n), device=lhs.device, dtype=torch.uint8 if fp8_out else out_dtype)
+    if m and n:
+        def arg(t):
+            return t.view(torch.uint8) if t.dtype in (torch.float8_e4m3fn, torch.float8_e5m2) else t
+        a, b = arg(lhs), arg(rhs)
+        _lib.call("b200_matmul_generic", a.data_ptr(), _lib.DT[D.name(lhs.dtype)], lhs.stride(0), lhs.stride(1),
+                  b.data_ptr(), _lib.DT[D.name(rhs.dtype)], rhs.stride(0), rhs.stride(1), out.data_ptr(),
+                  _lib.DT[D.name(out_dtype)], out.stride(0), out.stride(1), m, n, k, _lib.DT[D.name(acc_dtype)],
+                  stream_ptr(lhs.device))
+    return out.view(out_dtype) if fp8_out else out
+
+
+def _fused_operands(a, b, out_dtype):
+    """The (W, x) pair for a fused call, or None when the fused kernels cannot take it."""
+    if not isinstance(a, PackedTensor) or isinstance(b, PackedTensor) or len(a.shape) != 2:
+        return None
+    if b.dtype not in FUSED_IO or out_dtype not in FUSED_IO:
+        return None
+    if a.scales is not None and D.name(a.scales.dtype) == "float64":
+        return None
+    return a, b.t()  # x[m, k] = b[k, m]
+
+
+def _aligned_x(x: torch.Tensor) -> torch.Tensor:
+    """Fused kernels read x rows with 16-byte vector loads: stage (copy) a strided or
+    misaligned view, as the reference stages unaligned matrix inputs (linalg.py:61-87)."""
+    es = x.element_size()
+
+    def ok(t: torch.Tensor) -> bool:
+        return t.stride(1) == 1 and t.data_ptr() % 16 == 0 and (t.shape[0] == 1 or (t.stride(0) * es) % 16 == 0)
+
+    if ok(x):
+        return x
+    y = x.contiguous()
+    if ok(y):
+        return y
+    k = x.shape[1]
+    kp = -(-k * es // 16) * 16 // es
+    buf = torch.zeros((x.shape[0], kp), dtype=x.dtype, device=x.device)
+    buf[:, :k] = x
+    return buf[:, :k]
+
+
+def _packed_linear(w: PackedTensor, x: torch.Tensor, out_dtype: torch.dtype, path: str) -> torch.Tensor:
+    """y[M, N] = x[M, K] @ dequant(W)[N, K]^T through ``b200_packed_linear``."""
+    x = _aligned_x(x)
+    m = x.shape[0]
+    ldx = x.stride(0) if m > 1 else -(-x.shape[1] // 8) * 8
+    y = torch.empty((m, w.rows), device=x.device, dtype=out_dtype)
+    d = w.desc()
+    _lib.call("b200_packed_linear", ctypes_ref(d), x.data_ptr(), _lib.DT[D.name(x.dtype)], m, ldx, 1,
+              y.data_ptr(), _lib.DT[D.name(out_dtype)], y.stride(0), 1, _lib.PATH[path], stream_ptr(x.device))
+    return y
+
+
+def linear_plan(w: PackedTensor, x_dtype: torch.dtype, m: int, out_dtype: torch.dtype, path: str = "auto") -> str | None:
+    """Name of the fused kernel the library would run ('gemv', 'gemm', 'simt') or None."""
+    d = w.desc()
+    rc = _lib.lib().b200_packed_linear_plan(ctypes_ref(d), _lib.DT[D.name(x_dtype)], m, _lib.DT[D.name(out_dtype)],
+                                            _lib.PATH[path])
+    return _lib.PATH_NAME.get(rc) if rc > 0 else None
+
+
+def choose_matrix(w: PackedTensor, x_dtype: torch.dtype, m: int, out_dtype: torch.dtype, scope: str = "auto"):
+    """Selected (scope, kernel) for these operands (linalg.py:90-133); 'tiled' means ordinary compute."""
+    if scope not in SCOPES:
+        raise ValueError(f"unknown matrix scope {scope!r}")
+    if scope == "tiled":
+        return ("tiled", None)
+    for path in _SCOPE_PATHS[scope]:
+        plan = linear_plan(w, x_dtype, m, out_dtype, path)
+        if plan is not None:
+            return ({"gemv": "Wave", "gemm": "ThreadGroup", "simt": "Wave"}[plan], plan)
+    return ("tiled", None)
+
+
+def matmul(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor, scope: str = "auto",
+           tile: tuple[int, int, int] | None = None, dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Multiply two matrices on the B200 device (linalg.py:136-223).
+
+    Packed operands decode inside the fused kernels; other combinations decode with
+    ``b200_dequant`` to the common intermediate and multiply with the generic kernel.
+    ``dtype`` declares the output precision (accumulation is float32 in the fused kernels,
+    the output dtype's reduction type in the generic one). No gradients are defined.
+    """
+    if scope not in SCOPES:
+        raise ValueError(f"unknown matrix scope {scope!r}")
+    automatic = scope == "auto"
+    device, other_device = _device_of(a), _device_of(b)
+    if device != other_device:
+        raise ValueError("matrix operands must belong to one device")
+    if len(a.shape) != 2 or len(b.shape) != 2 or a.shape[1] != b.shape[0]:
+        raise ValueError("matrix operands must have compatible rank-two shapes")
+    _check_cuda(device)
+    if tile is not None and any(x < 1 for x in tile):
+        raise ValueError("matrix tile dimensions must be positive")
+    intermediate = matrix_intermediate(a, b)
+    m, k, n = a.shape[0], a.shape[1], b.shape[1]
+    lhs_dt = intermediate if isinstance(a, PackedTensor) else a.dtype
+    rhs_dt = intermediate if isinstance(b, PackedTensor) else b.dtype
+    out_dtype = dtype or D.accumulator(lhs_dt, rhs_dt)
+    if 0 in (m, k, n):
+        return torch.zeros((m, n), device=device, dtype=out_dtype)
+    if scope != "tiled":
+        fused = _fused_operands(a, b, out_dtype)
+        if fused is not None:
+            w, x = fused
+            for path in _SCOPE_PATHS[scope]:
+                if linear_plan(w, x.dtype, x.shape[0], out_dtype, path) is not None:
+                    return _packed_linear(w, x, out_dtype, path).t()
+        if not automatic:
+            raise RuntimeError(f"B200 {scope} {tile} rejected: no fused kernel for these operands")
+    # ordinary compute: decode to the intermediate, then the generic matmul
+    wide = D.accumulator(intermediate, intermediate) if scope == "tiled" else intermediate
+    lhs = a.unpack(wide) if isinstance(a, PackedTensor) else a
+    rhs = b.unpack(wide) if isinstance(b, PackedTensor) else b
+    acc = D.sum_acc_dtype(out_dtype) if D.is_float(out_dtype) else out_dtype
+    return _generic_matmul(lhs, rhs, out_dtype, acc)
+
+
+def matvec(matrix: torch.Tensor | PackedTensor, vector: torch.Tensor, output_dtype: torch.dtype | None = None,
+           thread: bool | None = None) -> torch.Tensor:
+    """Matrix-vector product (linalg.py:226-298).
+
+    ``thread=None`` is a one-column ``matmul``. ``thread=True`` requests the warp-scope
+    decode GEMV (the B200 counterpart of the reference's thread-scope matrix API) and falls
+    back to ordinary compute when it cannot run; ``thread=False`` selects ordinary compute.
+    """
+    device = _device_of(matrix)
+    if len(matrix.shape) != 2 or vector.dim() != 1 or matrix.shape[1] != vector.shape[0] or device != vector.device:
+        raise ValueError("matvec expects a matrix and matching vector on one device")
+    intermediate = matrix_intermediate(matrix, vector)
+    output_dtype = output_dtype or D.accumulator(intermediate, intermediate)
+    if thread is None:
+        return matmul(matrix, vector.reshape(-1, 1), dtype=output_dtype).reshape(matrix.shape[0])
+    if thread:
+        try:
+            return matmul(matrix, vector.reshape(-1, 1), scope="Wave", dtype=output_dtype).reshape(matrix.shape[0])
+        except RuntimeError as error:
+            if "rejected" not in str(error):
+                raise
+    return matmul(matrix, vector.reshape(-1, 1), scope="tiled", dtype=output_dtype).reshape(matrix.shape[0])

@@ -1,0 +1,175 @@
+"""Packed low-bit tensors on the B200 device.
+
+Drop-in for tinygrad-dx12 ``src/tinygrad_dx12/codegen/decomp/dx12.py``: the same
+``FORMATS`` / ``FP8_CANDIDATES`` tables (:10-11), the same ``PackedTensor`` fields,
+validation and byte layout (:14-47), the same ``unpack`` dtype rules (:49-106), the same
+``matrix_intermediate`` selection (:115-138) and the decomp ``matmul`` helper (:141-149).
+Tensors are torch CUDA tensors; decoding runs in the library's ``b200_dequant`` kernel.
+There is no CPU path: a packed operand on any other device is rejected.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from . import dtypes as D
+
+# (total bits, exponent bits, mantissa bits, exponent bias); integers have no exponent.
+FORMATS = {"int4": (4, 0, 0, 0), "uint4": (4, 0, 0, 0), "fp4_e2m1": (4, 2, 1, 1), "fp6_e2m3": (6, 2, 3, 1),
+           "fp6_e3m2": (6, 3, 2, 3)}
+FP8_CANDIDATES = {"fp4_e2m1": (torch.float8_e4m3fn, torch.float8_e5m2), "fp6_e2m3": (torch.float8_e4m3fn,),
+                  "fp6_e3m2": (torch.float8_e4m3fn, torch.float8_e5m2)}
+
+
+def _require_cuda(t: torch.Tensor, what: str) -> None:
+    if t.device.type != "cuda":
+        raise ValueError(f"{what} must be a CUDA tensor on the B200 device, not {t.device}")
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+@dataclass(frozen=True)
+class PackedTensor:
+    """A contiguous low-bit tensor stored least-significant payload first in bytes.
+
+    ``shape`` gives the logical elements and ``data`` is a flat uint8 tensor. Six-bit
+    elements may straddle bytes. FP4 and FP6 use finite OCP payloads. Optional numeric
+    ``scales`` have shape ``shape[:-1] + (ceil(K/block_size),)``; each scale applies to
+    one block along the final dimension. A ``torch.float8_e8m0fnu`` scale tensor is read
+    as the power of two it encodes.
+    """
+
+    data: torch.Tensor
+    format: str
+    shape: tuple
+    scales: torch.Tensor | None = None
+    block_size: int = 32
+
+    def __post_init__(self) -> None:
+        """Reject missing format metadata, insufficient storage, and incompatible scales (dx12.py:32-47)."""
+        object.__setattr__(self, "shape", tuple(int(s) for s in self.shape))
+        if self.format not in FORMATS:
+            raise ValueError(f"unknown packed format {self.format!r}")
+        if not self.shape or any(x < 0 for x in self.shape):
+            raise ValueError("packed shape must contain nonnegative dimensions")
+        if not isinstance(self.data, torch.Tensor) or self.data.dtype is not torch.uint8 or self.data.dim() != 1:
+            raise ValueError("packed data must be a flat uint8 Tensor")
+        if self.data.numel() < (math.prod(self.shape) * FORMATS[self.format][0] + 7) // 8:
+            raise ValueError("packed storage is smaller than the declared shape")
+        if self.block_size < 1:
+            raise ValueError("packed block size must be positive")
+        if self.scales is not None:
+            expected = self.shape[:-1] + ((self.shape[-1] + self.block_size - 1) // self.block_size,)
+            if tuple(self.scales.shape) != expected or self.scales.device != self.data.device:
+                raise ValueError("packed scales have incompatible shape or device")
+
+    # ---- helpers -----------------------------------------------------------------------
+    @property
+    def device(self) -> torch.device:
+        return self.data.device
+
+    @property
+    def dtype(self) -> torch.dtype:
+        """Declared numeric type used by matrix_intermediate (dx12.py:131-136)."""
+        if self.scales is not None:
+            return D.least_upper_dtype(torch.float32, self.scales.dtype)
+        return {"int4": torch.int8, "uint4": torch.uint8}.get(self.format, torch.float16)
+
+    @property
+    def rows(self) -> int:
+        return math.prod(self.shape[:-1])
+
+    @property
+    def cols(self) -> int:
+        return self.shape[-1]
+
+    def desc(self) -> _lib.PackedDesc:
+        """The C-ABI descriptor (rows = prod(shape[:-1]), cols = shape[-1])."""
+        _require_cuda(self.data, "packed data")
+        data = self.data if self.data.is_contiguous() else self.data.contiguous()
+        scales = None
+        if self.scales is not None:
+            scales = self.scales if self.scales.is_contiguous() else self.scales.contiguous()
+        d = _lib.PackedDesc()
+        d.data = data.data_ptr() if data.numel() else None
+        d.data_bytes = data.numel()
+        d.format = _lib.FMT[self.format]
+        d.scale_dtype = _lib.DT[D.code_name(scales.dtype)] if scales is not None else 0
+        d.rows, d.cols, d.block_size = self.rows, self.cols, self.block_size
+        d.scales = scales.data_ptr() if scales is not None and scales.numel() else None
+        d._keep = (data, scales)  # keep contiguous copies alive for the call
+        return d
+
+    def default_dtype(self) -> torch.dtype:
+        """dx12.py:57-64."""
+        integer = self.format in ("int4", "uint4")
+        if self.scales is not None:
+            return D.least_upper_dtype(torch.float32, self.scales.dtype)
+        return torch.int32 if integer else torch.float32
+
+    def unpack(self, dtype: torch.dtype | None = None) -> torch.Tensor:
+        """Decode to numeric elements and apply scales at their original K boundaries.
+
+        Floating payloads and scaled integers default to float32 (float64 with float64
+        scales); unscaled integers default to int32. Unscaled, exactly representable FP8
+        destinations use the direct encoding of dx12.py:78-92. Runs ``b200_dequant``.
+        """
+        dtype = dtype or self.default_dtype()
+        _require_cuda(self.data, "packed data")
+        count = math.prod(self.shape)
+        fp8 = dtype in (torch.float8_e4m3fn, torch.float8_e5m2)
+        out = torch.empty(self.shape, device=self.device, dtype=torch.uint8 if fp8 else dtype)
+        if count:
+            d = self.desc()
+            _lib.call("b200_dequant", ctypes_ref(d), 0, count, out.data_ptr(), _lib.DT[D.name(dtype)],
+                      stream_ptr(self.device))
+        return out.view(dtype) if fp8 else out
+
+    def matmul(self, other: torch.Tensor | "PackedTensor") -> torch.Tensor:
+        """The explicit matrix API (dx12.py:108-112 -> codegen/linalg.py:136)."""
+        from .linalg import matmul
+
+        return matmul(self, other)
+
+
+def ctypes_ref(d: _lib.PackedDesc):
+    import ctypes
+
+    return ctypes.byref(d)
+
+
+def matrix_intermediate(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor, native16: bool = False) -> torch.dtype:
+    """Shared dtype promotion after selecting an exact packed storage representation (dx12.py:115-138).
+
+    Prefer a common FP8 encoding when both operands fit; otherwise promote the declared
+    types. ``native16`` is accepted for signature compatibility and changes nothing.
+    """
+    operands = (a, b)
+    candidates = set.intersection(*[
+        {op.dtype} if isinstance(op, torch.Tensor)
+        else set(FP8_CANDIDATES.get(op.format, ())) if op.scales is None else set()
+        for op in operands
+    ])
+    for dt in (torch.float8_e4m3fn, torch.float8_e5m2):
+        if dt in candidates:
+            return dt
+    return D.least_upper_dtype(*[op.dtype for op in operands])
+
+
+def matmul(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor) -> torch.Tensor:
+    """Decomp helper (dx12.py:141-149): unpack with default dtypes, then an ordinary matmul.
+
+    The ordinary matmul is the library's generic kernel (no fused decode), accumulating in
+    tinygrad's default reduction dtype of the two operand types.
+    """
+    from .linalg import _generic_matmul
+
+    lhs, rhs = [op.unpack() if isinstance(op, PackedTensor) else op for op in (a, b)]
+    out_dtype = D.least_upper_dtype(lhs.dtype, rhs.dtype)
+    return _generic_matmul(lhs, rhs, out_dtype, D.sum_acc_dtype(out_dtype))
