@@ -185,16 +185,18 @@ def run_gpu_arm(args, world, rank, local):
     with torch.cuda.graph(graph, stream=stream):
         for i in range(args.steps):
             launch(args.warmup + i, stream.cuda_stream)
-    graph.replay()  # one untimed replay (graph upload)
+    with torch.cuda.stream(stream):
+        graph.replay()  # one untimed replay (graph upload)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
-        ev0.record(stream)
-        graph.replay()
-        ev1.record(stream)
+        with torch.cuda.stream(stream):  # replay() launches on the current stream
+            ev0.record(stream)
+            graph.replay()
+            ev1.record(stream)
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()

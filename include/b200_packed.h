@@ -155,6 +155,11 @@ int32_t b200_event_record(void *event, void *stream);
 int32_t b200_event_elapsed_ms(void *start, void *end, float *ms);
 int32_t b200_event_destroy(void *event);
 
+/* Sticky device-side error bits of the library's kernels on `device` (bit 0: a bounded
+ * mbarrier / flag wait gave up and the kernel returned early). Synchronous; `clear` != 0
+ * resets them. Replaces the sticky `failure` of runtime/ops_dx12.py:171,195-198. */
+int32_t b200_device_status(int32_t device, uint32_t *flags, int32_t clear);
+
 /* Device-side bounded wait (failure detection without a GPU fault): a one-thread kernel
  * spins until *flag == expect or `max_spins` polls have passed, then writes 0 (seen) or
  * B200_ERR_TIMEOUT to *status. Never traps. */

@@ -46,6 +46,16 @@ def oracle_scales(spec: ref.PackedSpec, scale_dtype: str | None):
     return cast, scale_dtype
 
 
+def to_numpy(t: torch.Tensor) -> np.ndarray:
+    """Host copy of a device tensor, including bf16 / fp8 (returned as ml_dtypes arrays)."""
+    t = t.detach().cpu()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(ref.BF16)
+    if t.dtype in (torch.float8_e4m3fn, torch.float8_e5m2):
+        return t.view(torch.uint8).numpy().view(ref.FP8E4M3 if t.dtype == torch.float8_e4m3fn else ref.FP8E5M2)
+    return t.numpy()
+
+
 def errors(y: np.ndarray, r: np.ndarray) -> tuple[float, float]:
     y = y.astype(np.float64)
     r = r.astype(np.float64)

@@ -8,7 +8,7 @@ import pytest
 import torch
 
 from oracle import packed_ref as ref
-from tests.helpers import bits_equal, to_device, TORCH_OF
+from tests.helpers import bits_equal, to_device, to_numpy, TORCH_OF
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -51,7 +51,7 @@ def test_dequant_bit_exact(fmt, scale, shape, bs):
     if scale not in (None, "e8m0"):
         spec = ref.PackedSpec(spec.data, fmt, shape, spec.scales.astype(ref.np_dtype(scale)), bs)
     w = to_device(spec, DEV, scale)
-    got = w.unpack().cpu().numpy()
+    got = to_numpy(w.unpack())
     exp = ref.dequant(spec.data, fmt, shape, spec.scales, bs, None, spec.scale_dtype)
     assert got.dtype == exp.dtype
     assert bits_equal(got, exp)
@@ -64,12 +64,12 @@ def test_dequant_explicit_dtype(fmt, dtype):
     spec = ref.make_packed(rng, fmt, 16, 64, 32, "f16u")
     w = to_device(spec, DEV)
     tdt = {"int32": torch.int32, **TORCH_OF}[dtype]
-    got = w.unpack(tdt).cpu().numpy()
+    got = to_numpy(w.unpack(tdt))
     exp = ref.dequant(spec.data, fmt, (16, 64), spec.scales, 32, dtype)
     assert bits_equal(got, exp)
     # unscaled too
     w0 = to_device(ref.PackedSpec(spec.data, fmt, (16, 64)), DEV)
-    assert bits_equal(w0.unpack(tdt).cpu().numpy(), ref.dequant(spec.data, fmt, (16, 64), dtype=dtype))
+    assert bits_equal(to_numpy(w0.unpack(tdt)), ref.dequant(spec.data, fmt, (16, 64), dtype=dtype))
 
 
 @pytest.mark.parametrize("fmt,target", [(f, t) for f, ts in ref.FP8_CANDIDATES.items() for t in ts])

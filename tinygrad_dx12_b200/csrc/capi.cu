@@ -277,6 +277,15 @@ int32_t b200_event_destroy(void *event) {
   return B200_OK;
 }
 
+int32_t b200_device_status(int32_t device, uint32_t *flags, int32_t clear) {
+  if (flags == nullptr) return b200_set_error(B200_ERR_INVALID, "null flags");
+  B200_CUDA_TRY(cudaSetDevice(device));
+  unsigned int v = 0;
+  if (int32_t rc = gemm_device_error(&v, clear != 0)) return rc;
+  *flags = v;
+  return B200_OK;
+}
+
 int32_t b200_device_wait_flag(const int32_t *flag, int32_t expect, int64_t max_spins, int32_t *status, void *stream) {
   if (flag == nullptr || status == nullptr) return b200_set_error(B200_ERR_INVALID, "null flag/status");
   if (max_spins < 0) return b200_set_error(B200_ERR_INVALID, "max_spins must be bounded");

@@ -36,6 +36,7 @@ int32_t launch_gemv_tc(const LinearArgs &a, cudaStream_t stream);
 // tcgen05 GEMM (M > 32; x f16/bf16).
 bool gemm_supported(const LinearArgs &a);
 int32_t launch_gemm(const LinearArgs &a, cudaStream_t stream);
+int32_t gemm_device_error(unsigned int *v, bool clear);
 
 int32_t launch_matmul_generic(const void *a, int adt, int64_t sam, int64_t sak, const void *b, int bdt, int64_t sbk,
                               int64_t sbn, void *c, int cdt, int64_t scm, int64_t scn, int64_t M, int64_t N, int64_t K,
