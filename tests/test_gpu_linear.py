@@ -27,13 +27,17 @@ _WCACHE: dict = {}
 
 
 def _wref(spec, scale_dtype):
+    """float32 oracle weights; cached per live spec object (the entry holds the spec so its
+    id cannot be reused by another object while cached)."""
     key = (id(spec), scale_dtype)
-    if key not in _WCACHE:
+    hit = _WCACHE.get(key)
+    if hit is None or hit[0] is not spec:
         if len(_WCACHE) > 4:
             _WCACHE.clear()
         sc, sdt = oracle_scales(spec, scale_dtype)
-        _WCACHE[key] = ref.dequant(spec.data, spec.format, spec.shape, sc, spec.block_size, "float32", sdt)
-    return _WCACHE[key]
+        hit = (spec, ref.dequant(spec.data, spec.format, spec.shape, sc, spec.block_size, "float32", sdt))
+        _WCACHE[key] = hit
+    return hit[1]
 
 
 def _run(spec, scale_dtype, m, xdt, ydt, path="auto", seed=0, xscale=1.0):
