@@ -71,6 +71,12 @@ extern "C" {
 #define B200_PATH_GEMV 1    /* force the fused decode GEMV                              */
 #define B200_PATH_GEMM 2    /* force the tcgen05 GEMM                                   */
 #define B200_PATH_SIMT 3    /* force the fp32 CUDA-core fused kernel                    */
+/* OR-able flag: launch with programmatic dependent launch (PDL). The kernel may start while
+ * the previous kernel on the stream is still running; it streams its packed weights and
+ * scales at once and waits for that kernel before it reads x or writes y. Only valid when
+ * the weights and scales are not written by the immediately preceding kernels (true for
+ * inference weights); the activation dependency is always honoured. */
+#define B200_FLAG_PDL 0x100
 
 /*
  * Packed operand descriptor: the fields of PackedTensor (codegen/decomp/dx12.py:26-30)

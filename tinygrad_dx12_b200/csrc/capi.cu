@@ -126,11 +126,13 @@ static bool fill_linear(const b200_packed_desc *w, const void *x, int32_t x_dtyp
   a.ydt = y_dtype;
   a.ldy_m = y_stride_m;
   a.ldy_n = y_stride_n;
+  a.flags = 0;
   return x_stride_k == 1;
 }
 
 static int32_t plan(const LinearArgs &a, bool kstride_ok, int32_t path) {
   if (!kstride_ok) return B200_ERR_UNSUPPORTED;
+  path &= 0xFF;  // flag bits (B200_FLAG_*) do not select a kernel
   const bool tc = gemv_tc_supported(a), gm = gemm_supported(a), simt = simt_supported(a);
   switch (path) {
     case B200_PATH_AUTO:
@@ -163,10 +165,11 @@ int32_t b200_packed_linear(const b200_packed_desc *w, const void *x, int32_t x_d
   if (x == nullptr || y == nullptr) return b200_set_error(B200_ERR_INVALID, "null x or y");
   LinearArgs a;
   const bool ks = fill_linear(w, x, x_dtype, m, x_stride_m, x_stride_k, y, y_dtype, y_stride_m, y_stride_n, a);
+  a.flags = path & ~0xFF;
   const int32_t p = plan(a, ks, path);
   cudaStream_t s = (cudaStream_t)stream;
   switch (p) {
-    case B200_PATH_GEMV: return launch_gemv_tc(a, s);
+    case B200_PATH_GEMV: return gemv_stream_supported(a) ? launch_gemv_stream(a, s) : launch_gemv_tc(a, s);
     case B200_PATH_GEMM: return launch_gemm(a, s);
     case B200_PATH_SIMT: return launch_gemv_simt(a, s);
   }
@@ -280,9 +283,10 @@ int32_t b200_event_destroy(void *event) {
 int32_t b200_device_status(int32_t device, uint32_t *flags, int32_t clear) {
   if (flags == nullptr) return b200_set_error(B200_ERR_INVALID, "null flags");
   B200_CUDA_TRY(cudaSetDevice(device));
-  unsigned int v = 0;
+  unsigned int v = 0, u = 0;
   if (int32_t rc = gemm_device_error(&v, clear != 0)) return rc;
-  *flags = v;
+  if (int32_t rc = gemv_device_error(&u, clear != 0)) return rc;
+  *flags = v | u;
   return B200_OK;
 }
 

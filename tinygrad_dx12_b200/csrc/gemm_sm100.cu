@@ -274,9 +274,24 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+}  // namespace gemm
+
+int32_t make_tma_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
+                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
+
+namespace gemm {
+
 static int32_t make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
                         uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
-  auto fn = encode_fn();
+  return make_tma_2d(map, dt, base, inner, outer, row_bytes, box_inner, box_outer, swz);
+}
+
+}  // namespace gemm
+
+// 2-D tiled tensor map (no interleave, L2 256-byte promotion, zero fill out of bounds).
+int32_t make_tma_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
+                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+  auto fn = gemm::encode_fn();
   if (!fn) return b200_set_error(B200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {row_bytes};
@@ -287,6 +302,8 @@ static int32_t make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *ba
   if (r != CUDA_SUCCESS) return b200_set_error(B200_ERR_CUDA, "cuTensorMapEncodeTiled failed: %d", (int)r);
   return B200_OK;
 }
+
+namespace gemm {
 
 static float place_factor(int fmt, bool bf16) {
   // The generic pack2 decode produces true values; no placement factor in this kernel.

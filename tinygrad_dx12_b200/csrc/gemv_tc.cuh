@@ -42,6 +42,7 @@ struct Params {
   void *y;
   int ydt;
   int64_t ldy_m, ldy_n;
+  int pdl;  // launched with programmatic stream serialization
 };
 
 // ---- decode 8 payloads into 4 fp16 pairs (payload i, payload i+4) --------------------------
@@ -196,7 +197,8 @@ template <int FMT, int SK>
 __device__ __forceinline__ void compute_chunk(const Chunk<Fmt<FMT>::bits> &r, const __half *xblk, float &acc_a,
                                               float &acc_b) {
   constexpr int BITS = Fmt<FMT>::bits;
-  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  // two independent accumulator chains halve the serial mma latency of a chunk
+  float d[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int u = 0; u < 4; ++u) {  // 8-payload unit u of this lane's block
     uint32_t pa[4], pb[4];
@@ -208,13 +210,15 @@ __device__ __forceinline__ void compute_chunk(const Chunk<Fmt<FMT>::bits> &r, co
       decode8_6bit<FMT>((((uint64_t)r.a[wi + 1] << 32) | r.a[wi]) >> sh, pa);
       decode8_6bit<FMT>((((uint64_t)r.b[wi + 1] << 32) | r.b[wi]) >> sh, pb);
     }
-    // x of this unit (permuted): pairs (0,4),(1,5) then (2,6),(3,7); a zero slot for non-owners
+    // x of this unit in decode pair order; a zero slot for non-owner lanes
     const uint4 xv = *reinterpret_cast<const uint4 *>(xblk + 8 * u);
     const uint32_t a0[4] = {pa[0], pb[0], pa[1], pb[1]};
     mma16816(d, a0, xv.x, xv.y);
     const uint32_t a1[4] = {pa[2], pb[2], pa[3], pb[3]};
-    mma16816(d, a1, xv.z, xv.w);
+    mma16816(e, a1, xv.z, xv.w);
   }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d[i] += e[i];
   // d = {D[g][2t], D[g][2t+1], D[g+8][2t], D[g+8][2t+1]}: per-block partial sums
   if constexpr (SK == SK_NONE || SK == SK_ROW) {
     acc_a += d[0] + d[1];
@@ -280,12 +284,20 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_bd_kernel(Params p, int xbf16
   const uint8_t *wa = p.w + ra * row_bytes, *wb = p.w + rb * row_bytes;
   const int cm = t >> 1, cblk = 2 * (t & 1);  // accumulator columns 2t, 2t+1 -> (m, blocks)
 
-  // weights do not depend on x: start streaming them before staging x
+  // Programmatic dependent launch: let the next kernel in the stream start its own weight
+  // prefetch now (no-op unless it was launched with programmatic stream serialization).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  // weights and scales are parameters, not outputs of earlier kernels: start streaming them
+  // before waiting on the previous kernel and before staging x
   Chunk<BITS> ring[PF];
 #pragma unroll
   for (int j = 0; j < PF; ++j)
     if (c_begin + j < c_end) load_chunk<BITS, SK>(ring[j], p, wa, wb, c_begin + j, t, cblk, ra, rb);
 
+  // x may be the previous kernel's output and y may still be read by it: wait for it to
+  // finish (returns at once when this launch has no programmatic dependency)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (tid < CHUNK / 8) reinterpret_cast<uint4 *>(zslot)[tid] = make_uint4(0u, 0u, 0u, 0u);
   float prescale = 1.f;
   const bool ok = stage_x<pairs_04<FMT>()>(p, xs, K, xbf16 != 0, prescale);
@@ -352,8 +364,17 @@ static int32_t launch_t(const Params &p, bool xbf16, cudaStream_t stream) {
     attr = true;
   }
   const unsigned grid = (unsigned)((p.rows + ROWS - 1) / ROWS);
-  gemv_bd_kernel<FMT, SK><<<grid, WARPS * 32, smem, stream>>>(p, xbf16 ? 1 : 0);
-  B200_LAUNCH_CHECK();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(WARPS * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = p.pdl ? 1 : 0;
+  B200_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_bd_kernel<FMT, SK>, p, xbf16 ? 1 : 0));
   return B200_OK;
 }
 
@@ -423,6 +444,7 @@ int32_t launch_gemv_tc(const LinearArgs &a, cudaStream_t stream) {
   p.ydt = a.ydt;
   p.ldy_m = a.ldy_m;
   p.ldy_n = a.ldy_n;
+  p.pdl = (a.flags & B200_FLAG_PDL) ? 1 : 0;
   const bool bf = a.xdt == B200_DT_BF16;
   const int sk = scale_kind(a);
   switch (a.fmt) {

@@ -1,6 +1,7 @@
 // kernels.h -- host-side launchers shared between the C-ABI (capi.cu) and kernel files.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -20,6 +21,7 @@ struct LinearArgs {
   void *y;
   int ydt;
   int64_t ldy_m, ldy_n;
+  int flags;  // B200_FLAG_* bits
 };
 
 int32_t launch_dequant(const b200_packed_desc *w, int64_t begin, int64_t count, void *out, int32_t out_dtype,
@@ -37,6 +39,15 @@ int32_t launch_gemv_tc(const LinearArgs &a, cudaStream_t stream);
 bool gemm_supported(const LinearArgs &a);
 int32_t launch_gemm(const LinearArgs &a, cudaStream_t stream);
 int32_t gemm_device_error(unsigned int *v, bool clear);
+
+// 2-D tiled TMA descriptor (defined in gemm_sm100.cu); base 16-byte aligned, row_bytes % 16 == 0.
+int32_t make_tma_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
+                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
+
+// streamed (TMA) decode GEMV for M <= 2 (gemv.cu)
+bool gemv_stream_supported(const LinearArgs &a);
+int32_t launch_gemv_stream(const LinearArgs &a, cudaStream_t stream);
+int32_t gemv_device_error(unsigned int *v, bool clear);
 
 int32_t launch_matmul_generic(const void *a, int adt, int64_t sam, int64_t sak, const void *b, int bdt, int64_t sbk,
                               int64_t sbn, void *c, int cdt, int64_t scm, int64_t scn, int64_t M, int64_t N, int64_t K,
