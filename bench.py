@@ -169,9 +169,13 @@ def run_gpu_arm(args, world, rank, local):
     fn = _lib.lib().b200_packed_linear
     xdt_code, ydt_code = _lib.DT[cfg["xdt"]], _lib.DT[cfg["xdt"]]
 
+    # B200_FLAG_PDL: each step's kernel may start streaming its (parameter) weights while the
+    # previous step finishes; it still waits for the previous kernel before reading x / writing y
+    pdl = 0x100
+
     def launch(i, stream):
         rc = fn(ctypes.byref(descs[i % copies]), x.data_ptr(), xdt_code, cfg["m"], cfg["k"], 1, y.data_ptr(),
-                ydt_code, cfg["n"], 1, 0, stream)
+                ydt_code, cfg["n"], 1, pdl, stream)
         if rc:
             raise RuntimeError(_lib.last_error())
 
@@ -256,6 +260,8 @@ def run_gpu_arm(args, world, rank, local):
                        "weight_copies": copies, "l2": "inputs larger than L2: rotating %d weight copies (%.0f MB)" % (
                            copies, copies * bytes_step / 1e6),
                        "timing": "CUDA graph of K launches, CUDA events on the launch stream",
+                       "launch": "programmatic dependent launch (B200_FLAG_PDL): weights prefetched while the "
+                                 "previous step drains; x read / y written only after it completes",
                        "parallelism": f"independent weights per GPU x{world}"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,

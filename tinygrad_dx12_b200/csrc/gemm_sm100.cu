@@ -30,6 +30,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
+#include "decode.cuh"
 
 namespace b200 {
 
@@ -186,21 +187,23 @@ __global__ void __launch_bounds__(THREADS, 1)
           gf[g] = e8m0_to_f32(((const uint8_t *)p.scales)[n * p.nblk + (kb * BK + 32 * g) / p.block]);
       }
       uint8_t *dst = bsm + s * B_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
+      const bool scaled = p.scale_mode == SCALE_E8M0;
 #pragma unroll
-      for (int c = 0; c < BK / 8; ++c) {  // 16-byte chunk = 8 payloads
+      for (int c = 0; c < BK / 8; ++c) {  // 16-byte chunk = 8 payloads, natural K order
         uint32_t out[4];
+        gemv::decode8_natural<FMT, BF16>(w, c, out);
+        if (scaled) {  // power-of-two block scale: exact while the product stays in range
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int i0 = c * 8 + 2 * j;
-          uint32_t c0, c1;
-          if constexpr (BITS == 4) {
-            c0 = (w[i0 >> 3] >> ((i0 & 7) * 4)) & 0xFu;
-            c1 = (w[i0 >> 3] >> (((i0 & 7) + 1) * 4)) & 0xFu;
-          } else {
-            c0 = bits6(w, i0 * 6);
-            c1 = bits6(w, i0 * 6 + 6);
+          for (int j = 0; j < 4; ++j) {
+            if constexpr (BF16) {
+              const __nv_bfloat162 r = __hmul2(*reinterpret_cast<const __nv_bfloat162 *>(&out[j]),
+                                               __float2bfloat162_rn(gf[c >> 2]));
+              out[j] = *reinterpret_cast<const uint32_t *>(&r);
+            } else {
+              const __half2 r = __hmul2(*reinterpret_cast<const __half2 *>(&out[j]), __float2half2_rn(gf[c >> 2]));
+              out[j] = *reinterpret_cast<const uint32_t *>(&r);
+            }
           }
-          out[j] = pack2<FMT, BF16>(c0, c1, gf[c >> 2]);
         }
         *reinterpret_cast<uint4 *>(dst + ((c ^ (t & 7)) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
       }
