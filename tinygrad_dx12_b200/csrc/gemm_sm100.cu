@@ -6,25 +6,27 @@
 // src/tinygrad_dx12/renderer/linalg.py:38-124) for packed operands, with the decode of
 // src/tinygrad_dx12/codegen/decomp/dx12.py:69-106 fused on chip instead of materialised.
 //
-// One CTA computes a 128 (m) x 128 (n) output tile; K advances 64 elements per stage through a
-// 4-stage shared-memory ring:
-//   warp 0 lane 0  TMA producer: x tile (128 x 64, 128-byte swizzle) and the packed weight
-//                  bytes of the tile (128 rows x 32/48 bytes), both signalled on full[s];
-//   warp 1 lane 0  MMA issuer: 4 x tcgen05.mma.kind::f16 (M=128, N=128, K=16) per stage into a
-//                  128-column fp32 TMEM accumulator; tcgen05.commit frees the stage (empty[s]);
+// Persistent kernel: one CTA per SM walks 128 (m) x 128 (n) output tiles; K advances 64
+// elements per stage through a 4-stage shared-memory ring that runs continuously across tiles.
+//   warp 0 lane 0  TMA producer: x tile (128 x 64, 128-byte swizzle) and the tile's packed weight
+//                  bytes (128 rows x 32/48 bytes), both signalled on full[s];
+//   warp 1 lane 0  MMA issuer: 4 x tcgen05.mma.kind::f16 (M=128, N=128, K=16) per stage into one
+//                  of two 128-column fp32 TMEM accumulators; tcgen05.commit frees the stage
+//                  (empty[s]) and, after the last stage of a tile, publishes the accumulator;
 //   warps 2..5     dequant warpgroup: each thread decodes one weight row of the stage (64
-//                  payloads) to fp16/bf16 -- exact, see below -- and writes it in the 128-byte
-//                  swizzled K-major layout the MMA reads (bready[s]); after the K loop the same
-//                  warps are the epilogue: tcgen05.ld, per-column scale, cast, store.
+//                  payloads) to exact fp16/bf16 (decode.cuh) and writes it in the 128-byte
+//                  swizzled K-major layout the MMA reads (bready[s]);
+//   warps 6..9     epilogue warpgroup: tcgen05.ld of the finished accumulator, per-column scale,
+//                  cast, store; it frees the accumulator so the next-but-one tile can reuse it,
+//                  which overlaps each epilogue with the next tile's main loop.
 // Every mbarrier wait is bounded (sm100.cuh): on give-up the CTA drains its copies and MMAs,
 // frees TMEM and returns, and the library's device error flag is set.
 //
 // Exactness: every payload value is exactly representable in fp16 and bf16 (<= 4 significant
-// bits, small exponent range). Per-row scales (block_size >= K) and the power-of-two bit
-// placement factor multiply the fp32 accumulator in the epilogue; per-group E8M0 scales are
-// powers of two and multiply the operand exactly (barring fp16 overflow). Products are exact
-// in the fp32 accumulator, so results equal the reference's fp32 arithmetic up to summation
-// order.
+// bits, small exponent range). Per-row scales (block_size >= K) multiply the fp32 accumulator
+// in the epilogue; per-group E8M0 scales are powers of two and multiply the operand exactly
+// (barring fp16 overflow). Products are exact in the fp32 accumulator, so results equal the
+// reference's fp32 arithmetic up to summation order.
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -41,12 +43,14 @@ int32_t gemm_device_error(unsigned int *v, bool clear) {
 
 namespace gemm {
 
-constexpr int BM = 128, BN = 128, BK = 64, STAGES = 4, THREADS = 192;
+constexpr int BM = 128, BN = 128, BK = 64, STAGES = 4, ACC = 2;
+constexpr int DQ_WARPS = 8;           // dequant warps: two threads per weight row
+constexpr int THREADS = (2 + DQ_WARPS + 4) * 32;  // producer, MMA, dequant, 4 epilogue warps
 constexpr int X_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_BYTES = BN * BK * 2;  // 16 KB
 constexpr int P_STAGE = 6144;         // packed bytes slot (128 rows x 48 B max), 1024-aligned
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (X_BYTES + B_BYTES + P_STAGE) + 1024 /*bars etc*/ +
-                           BN * 4;
+                           ACC * BN * 4;
 enum ScaleMode { SCALE_NONE = 0, SCALE_ROW = 1, SCALE_E8M0 = 2 };
 
 struct Params {
@@ -55,34 +59,11 @@ struct Params {
   int sdt;
   int64_t nblk, block;
   int scale_mode;
-  float place;  // power-of-two factor of the bit placement, folded into the epilogue
   void *y;
   int ydt;
   int64_t ldy;
+  int mblocks, nblocks;  // tile grid
 };
-
-// ---- payload -> fp16 / bf16 bits (exact) -----------------------------------------------
-template <int FMT, bool BF16>
-__device__ __forceinline__ uint32_t pack2(uint32_t c0, uint32_t c1, float f) {
-  const float v0 = decode_f32<FMT>(c0) * f, v1 = decode_f32<FMT>(c1) * f;
-  if constexpr (BF16) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
-    return *reinterpret_cast<uint32_t *>(&h);
-  } else {
-    __half2 h = __floats2half2_rn(v0, v1);
-    return *reinterpret_cast<uint32_t *>(&h);
-  }
-}
-
-// 6-bit payload starting at bit b of a little-endian word array (b is a compile-time constant
-// after unrolling).
-template <int NW>
-__device__ __forceinline__ uint32_t bits6(const uint32_t (&w)[NW], int b) {
-  const int wi = b >> 5, sh = b & 31;
-  uint32_t v = w[wi] >> sh;
-  if (sh > 26) v |= w[wi + 1] << (32 - sh);
-  return v & 0x3Fu;
-}
 
 template <int FMT, bool BF16>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -98,135 +79,172 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t *full = (uint64_t *)(ps + STAGES * P_STAGE);
   uint64_t *bready = full + STAGES;
   uint64_t *empty = bready + STAGES;
-  uint64_t *accum = empty + STAGES;
-  uint32_t *tmem_slot = (uint32_t *)(accum + 1);
+  uint64_t *accf = empty + STAGES;  // [ACC] accumulator ready for the epilogue
+  uint64_t *acce = accf + ACC;      // [ACC] accumulator drained by the epilogue
+  uint64_t *done = acce + ACC;      // all MMAs of this CTA retired (exit path)
+  uint32_t *tmem_slot = (uint32_t *)(done + 1);
   volatile uint32_t *abort_flag = tmem_slot + 1;
-  float *colscale = (float *)(tmem_slot + 4);
+  float *colscale = (float *)(tmem_slot + 4);  // [ACC][BN]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
   const int nk = (int)(p.K / BK);
+  const int ntiles = p.mblocks * p.nblocks;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&bready[s], 128);
+      mbar_init(&bready[s], DQ_WARPS * 32);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int a = 0; a < ACC; ++a) {
+      mbar_init(&accf[a], 1);
+      mbar_init(&acce[a], 128);
+    }
+    mbar_init(done, 1);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmx);
     prefetch_tmap(&tmw);
   }
   __syncwarp();
-  if (warp == 0) tmem_alloc(tmem_slot, BN);
-  if (threadIdx.x >= 64) {
-    const int t = threadIdx.x - 64;
-    const int64_t n = n0 + t;
-    float s = p.place;
-    if (p.scale_mode == SCALE_ROW && n < p.N) s *= load_as_f32(p.scales, n * p.nblk, p.sdt);
-    colscale[t] = s;
-  }
+  if (warp == 0) tmem_alloc(tmem_slot, ACC * BN);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
+    // ---------------- TMA producer ----------------
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES, round = kb / STAGES;
-        if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&full[s], TX_BYTES);
-        tma_load_2d(xs + s * X_BYTES, &tmx, kb * BK, (int32_t)m0, &full[s]);
-        tma_load_2d(ps + s * P_STAGE, &tmw, kb * PB, (int32_t)n0, &full[s]);
-        issued = kb + 1;
+      int64_t q = 0, issued = 0;
+      for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const int mb = tile % p.mblocks, nb = tile / p.mblocks;
+        for (int kb = 0; kb < nk; ++kb, ++q) {
+          const int s = (int)(q % STAGES);
+          if (q >= STAGES && !mbar_wait(&empty[s], (uint32_t)((q / STAGES - 1) & 1), abort_flag)) continue;
+          if (*abort_flag) continue;
+          mbar_arrive_expect_tx(&full[s], TX_BYTES);
+          tma_load_2d(xs + s * X_BYTES, &tmx, kb * BK, mb * BM, &full[s]);
+          tma_load_2d(ps + s * P_STAGE, &tmw, kb * PB, nb * BN, &full[s]);
+          issued = q + 1;
+        }
       }
       if (*abort_flag) {  // drain this CTA's copies still in flight before it exits
-        for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; ++kb)
-          mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1, abort_flag, 200000000ull), (void)0;
+        for (int64_t r = (issued > STAGES ? issued - STAGES : 0); r < issued; ++r)
+          mbar_wait(&full[r % STAGES], (uint32_t)((r / STAGES) & 1), abort_flag, 200000000ull);
       }
     }
   } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16(BF16 ? 1u : 0u, BM, BN);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES, round = kb / STAGES;
-        if (!mbar_wait(&full[s], round & 1, abort_flag)) break;
-        if (!mbar_wait(&bready[s], round & 1, abort_flag)) break;
+      int64_t q = 0;
+      int i = 0;
+      for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++i) {
+        const int a = i & 1;
+        if (i >= ACC) mbar_wait(&acce[a], (uint32_t)((i / ACC - 1) & 1), abort_flag);
         tc_fence_after();
-        const uint64_t a0 = sw128_kmajor_desc(xs + s * X_BYTES);
-        const uint64_t b0 = sw128_kmajor_desc(bsm + s * B_BYTES);
+        const uint32_t dacc = tmem + (uint32_t)(a * BN);
+        for (int kb = 0; kb < nk; ++kb, ++q) {
+          const int s = (int)(q % STAGES);
+          const uint32_t ph = (uint32_t)((q / STAGES) & 1);
+          if (!mbar_wait(&full[s], ph, abort_flag) || !mbar_wait(&bready[s], ph, abort_flag)) continue;
+          tc_fence_after();
+          const uint64_t a0 = sw128_kmajor_desc(xs + s * X_BYTES);
+          const uint64_t b0 = sw128_kmajor_desc(bsm + s * B_BYTES);
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k)  // +32 bytes per K=16 step inside the swizzle atom
-          mma_f16_ss(tmem, a0 + (uint64_t)(2 * k), b0 + (uint64_t)(2 * k), idesc, (kb | k) != 0);
-        mma_commit(&empty[s]);
+          for (int k = 0; k < BK / 16; ++k)  // +32 bytes per K=16 step inside the swizzle atom
+            mma_f16_ss(dacc, a0 + (uint64_t)(2 * k), b0 + (uint64_t)(2 * k), idesc, (kb | k) != 0);
+          mma_commit(&empty[s]);
+        }
+        mma_commit(&accf[a]);  // arrives once this tile's MMAs have completed
       }
-      mma_commit(accum);  // arrives once every issued MMA has completed
+      mma_commit(done);
+      mbar_wait(done, 0, abort_flag, 500000000ull);
     }
-  } else {
-    // ---- dequant warpgroup ----
-    const int t = threadIdx.x - 64;  // weight row within the tile
-    const int64_t n = n0 + t;
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % STAGES, round = kb / STAGES;
-      if (!mbar_wait(&full[s], round & 1, abort_flag)) break;
-      const uint32_t *src = (const uint32_t *)(ps + s * P_STAGE + t * PB);
-      uint32_t w[PB / 4];
+  } else if (warp < 2 + DQ_WARPS) {
+    // ---------------- dequant warps: thread = (row t, half h) of the stage ----------------
+    const int dt = threadIdx.x - 64;
+    const int t = dt & (BN - 1), h = dt / BN;  // weight row within the tile, 32-payload half
+    const bool scaled = p.scale_mode == SCALE_E8M0;
+    int64_t q = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      const int64_t n = (int64_t)(tile / p.mblocks) * BN + t;
+      for (int kb = 0; kb < nk; ++kb, ++q) {
+        const int s = (int)(q % STAGES);
+        if (!mbar_wait(&full[s], (uint32_t)((q / STAGES) & 1), abort_flag)) continue;
+        const uint8_t *src = ps + s * P_STAGE + t * PB + h * (PB / 2);
+        uint32_t w[PB / 8];
+        if constexpr (BITS == 4) {
+          const uint4 u = *reinterpret_cast<const uint4 *>(src);
+          w[0] = u.x, w[1] = u.y, w[2] = u.z, w[3] = u.w;
+        } else {
 #pragma unroll
-      for (int i = 0; i < PB / 16; ++i) {
-        const uint4 u = *reinterpret_cast<const uint4 *>(src + 4 * i);
-        w[4 * i] = u.x, w[4 * i + 1] = u.y, w[4 * i + 2] = u.z, w[4 * i + 3] = u.w;
-      }
-      float gf[2] = {1.f, 1.f};
-      if (p.scale_mode == SCALE_E8M0 && n < p.N) {
-#pragma unroll
-        for (int g = 0; g < 2; ++g)
-          gf[g] = e8m0_to_f32(((const uint8_t *)p.scales)[n * p.nblk + (kb * BK + 32 * g) / p.block]);
-      }
-      uint8_t *dst = bsm + s * B_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
-      const bool scaled = p.scale_mode == SCALE_E8M0;
-#pragma unroll
-      for (int c = 0; c < BK / 8; ++c) {  // 16-byte chunk = 8 payloads, natural K order
-        uint32_t out[4];
-        gemv::decode8_natural<FMT, BF16>(w, c, out);
-        if (scaled) {  // power-of-two block scale: exact while the product stays in range
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if constexpr (BF16) {
-              const __nv_bfloat162 r = __hmul2(*reinterpret_cast<const __nv_bfloat162 *>(&out[j]),
-                                               __float2bfloat162_rn(gf[c >> 2]));
-              out[j] = *reinterpret_cast<const uint32_t *>(&r);
-            } else {
-              const __half2 r = __hmul2(*reinterpret_cast<const __half2 *>(&out[j]), __float2half2_rn(gf[c >> 2]));
-              out[j] = *reinterpret_cast<const uint32_t *>(&r);
-            }
+          for (int i = 0; i < 3; ++i) {
+            const uint2 u = *reinterpret_cast<const uint2 *>(src + 8 * i);
+            w[2 * i] = u.x, w[2 * i + 1] = u.y;
           }
         }
-        *reinterpret_cast<uint4 *>(dst + ((c ^ (t & 7)) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
+        float gf = 1.f;
+        if (scaled && n < p.N)
+          gf = e8m0_to_f32(((const uint8_t *)p.scales)[n * p.nblk + (kb * BK + 32 * h) / p.block]);
+        uint8_t *dst = bsm + s * B_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
+#pragma unroll
+        for (int cc = 0; cc < BK / 16; ++cc) {  // 16-byte chunk = 8 payloads, natural K order
+          const int c = h * (BK / 16) + cc;
+          uint32_t out[4];
+          gemv::decode8_natural<FMT, BF16>(w, cc, out);
+          if (scaled) {  // power-of-two block scale: exact while the product stays in range
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if constexpr (BF16) {
+                const __nv_bfloat162 r =
+                    __hmul2(*reinterpret_cast<const __nv_bfloat162 *>(&out[j]), __float2bfloat162_rn(gf));
+                out[j] = *reinterpret_cast<const uint32_t *>(&r);
+              } else {
+                const __half2 r = __hmul2(*reinterpret_cast<const __half2 *>(&out[j]), __float2half2_rn(gf));
+                out[j] = *reinterpret_cast<const uint32_t *>(&r);
+              }
+            }
+          }
+          *reinterpret_cast<uint4 *>(dst + ((c ^ (t & 7)) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&bready[s]);
       }
-      fence_proxy_async_smem();
-      mbar_arrive(&bready[s]);
     }
-    // ---- epilogue: TMEM -> registers -> scale -> y ----
-    const bool ok = mbar_wait(accum, 0, abort_flag);
-    if (ok && !*abort_flag) {
+  } else {
+    // ---------------- epilogue warpgroup ----------------
+    const int et = threadIdx.x - (2 + DQ_WARPS) * 32;  // 0..127
+    const int qd = warp & 3;           // TMEM lane quarter this warp may access
+    const int row = qd * 32 + lane;
+    const int esz = p.ydt == B200_DT_F32 ? 4 : 2;
+    const bool vec_ok = ((uintptr_t)p.y % 16 == 0) && ((p.ldy * esz) % 16 == 0);
+    int i = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++i) {
+      const int a = i & 1;
+      const int64_t m0 = (int64_t)(tile % p.mblocks) * BM, n0 = (int64_t)(tile / p.mblocks) * BN;
+      {
+        const int64_t n = n0 + et;
+        float s = 1.f;
+        if (p.scale_mode == SCALE_ROW && n < p.N) s = load_as_f32(p.scales, n * p.nblk, p.sdt);
+        colscale[a * BN + et] = s;
+      }
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      const bool ok = mbar_wait(&accf[a], (uint32_t)((i / ACC) & 1), abort_flag) && !*abort_flag;
       tc_fence_after();
-      const int q = warp & 3;
-      const int row = q * 32 + lane;
       const int64_t m = m0 + row;
-      const int esz = p.ydt == B200_DT_F32 ? 4 : 2;
-      const bool vec_ok = ((uintptr_t)p.y % 16 == 0) && ((p.ldy * esz) % 16 == 0) && p.ydt != B200_DT_F8E4M3;
+      const float *cs = colscale + a * BN;
       for (int c = 0; c < BN; c += 16) {
         uint32_t r[16];
-        tmem_ld_32x32b_x16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
-        tmem_ld_wait();
-        if (m < p.M) {
+        if (ok) {
+          tmem_ld_32x32b_x16(tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(a * BN + c), r);
+          tmem_ld_wait();
+        }
+        if (ok && m < p.M) {
           float v[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]) * colscale[c + j];
+          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]) * cs[c + j];
           const int64_t off = m * p.ldy + n0 + c;
           if (vec_ok && n0 + c + 16 <= p.N) {
             if (p.ydt == B200_DT_F32) {
@@ -256,12 +274,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
+      tc_fence_before();
+      mbar_arrive(&acce[a]);  // the accumulator may be overwritten by tile i + ACC
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, BN);
+  if (warp == 0) tmem_dealloc(tmem, ACC * BN);
 }
 
 // ---- host side ---------------------------------------------------------------------------
@@ -275,18 +295,6 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
       fn = (PFN_cuTensorMapEncodeTiled_v12000)ptr;
   }
   return fn;
-}
-
-}  // namespace gemm
-
-int32_t make_tma_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
-                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
-
-namespace gemm {
-
-static int32_t make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
-                        uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
-  return make_tma_2d(map, dt, base, inner, outer, row_bytes, box_inner, box_outer, swz);
 }
 
 }  // namespace gemm
@@ -308,28 +316,26 @@ int32_t make_tma_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, 
 
 namespace gemm {
 
-static float place_factor(int fmt, bool bf16) {
-  // The generic pack2 decode produces true values; no placement factor in this kernel.
-  (void)fmt;
-  (void)bf16;
-  return 1.f;
-}
-
 template <int FMT, bool BF16>
 static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
   constexpr int BITS = Fmt<FMT>::bits;
   static bool attr_set = false;
+  static int sms = 0;
   if (!attr_set) {
+    int dev = 0;
+    B200_CUDA_TRY(cudaGetDevice(&dev));
+    B200_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     B200_CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<FMT, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     attr_set = true;
   }
   CUtensorMap tmx, tmw;
-  if (int32_t rc = make_map(&tmx, BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x,
-                            (uint64_t)a.cols, (uint64_t)a.m, (uint64_t)a.ldx * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B))
+  if (int32_t rc = make_tma_2d(&tmx, BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x,
+                               (uint64_t)a.cols, (uint64_t)a.m, (uint64_t)a.ldx * 2, BK, BM,
+                               CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
   const uint64_t row_bytes = (uint64_t)a.cols * BITS / 8;
-  if (int32_t rc = make_map(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, row_bytes, (uint64_t)a.rows, row_bytes,
-                            BK * BITS / 8, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
+  if (int32_t rc = make_tma_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, row_bytes, (uint64_t)a.rows, row_bytes,
+                               BK * BITS / 8, BN, CU_TENSOR_MAP_SWIZZLE_NONE))
     return rc;
   Params p;
   p.M = a.m, p.N = a.rows, p.K = a.cols;
@@ -338,11 +344,13 @@ static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
   p.nblk = a.nblk;
   p.block = a.block;
   p.scale_mode = a.scales == nullptr ? SCALE_NONE : (a.block >= a.cols ? SCALE_ROW : SCALE_E8M0);
-  p.place = place_factor(FMT, BF16);
   p.y = a.y;
   p.ydt = a.ydt;
   p.ldy = a.ldy_m;
-  const dim3 grid((unsigned)((a.rows + BN - 1) / BN), (unsigned)((a.m + BM - 1) / BM));
+  p.mblocks = (int)((a.m + BM - 1) / BM);
+  p.nblocks = (int)((a.rows + BN - 1) / BN);
+  const int64_t tiles = (int64_t)p.mblocks * p.nblocks;
+  const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
   gemm_kernel<FMT, BF16><<<grid, THREADS, SMEM_BYTES, stream>>>(tmx, tmw, p);
   B200_LAUNCH_CHECK();
   return B200_OK;
@@ -355,7 +363,7 @@ bool gemm_supported(const LinearArgs &a) {
   if (a.xdt != B200_DT_F16 && a.xdt != B200_DT_BF16) return false;
   if (a.ydt != B200_DT_F16 && a.ydt != B200_DT_BF16 && a.ydt != B200_DT_F32) return false;
   if (a.cols < BK || a.cols % BK != 0 || a.rows <= 0 || a.m <= 0) return false;
-  if (a.m > 65535ll * BM || a.rows > (int64_t)INT32_MAX) return false;
+  if ((a.m + BM - 1) / BM * ((a.rows + BN - 1) / BN) > (int64_t)INT32_MAX) return false;
   if (a.ldy_n != 1) return false;
   if ((uintptr_t)a.w % 16 != 0 || (uintptr_t)a.x % 16 != 0 || (a.ldx * 2) % 16 != 0) return false;
   if (a.scales != nullptr) {
