@@ -1,10 +1,10 @@
 """Benchmark: packed GEMV HBM GB/s (M=1) and packed GEMM TFLOP/s (M=4096) on B200.
 
-Default workload (one "step"): BASELINE config 2 at M=1 -- y[1, 8192] = x[1, 8192] @ W^T with
+Default workload (one "step"): headline config c2 at M=1 -- y[1, 8192] = x[1, 8192] @ W^T with
 W an FP4 E2M1 (8192, 8192) packed matrix with per-32 E8M0 scales, bf16 x and y. Each step
 reads a different one of C resident weight copies (C * 35.7 MB > 4 x 126 MB L2), so every
 step streams its weights from HBM. The timed region replays a CUDA graph of exactly K
-packed-GEMV launches. A secondary measurement (key "gemm") times BASELINE config 3
+packed-GEMV launches. A secondary measurement (key "gemm") times headline config c3
 (FP6 E3M2, M=4096, K=4096, N=14336, per-row fp16 scales) in TFLOP/s.
 
 Multi-GPU (torchrun, one process per GPU): every rank runs the same per-GPU workload on its
@@ -36,10 +36,14 @@ import numpy as np  # noqa: E402
 L2_BYTES = 126 * 2**20
 GEMV_CFG = dict(fmt="fp4_e2m1", n=8192, k=8192, block=32, scale="e8m0", xdt="bfloat16", m=1)
 GEMM_CFG = dict(fmt="fp6_e3m2", n=14336, k=4096, block=4096, scale="f16row", xdt="float16", m=4096)
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of each timed kernel,
+# from one ncu capture of `bench.py --profile-case gemv|gemm` (profiles/gemv_stream_c2_m1.md,
+# profiles/gemm_c3_fp6.md). Refreshed whenever the kernel changes.
+NCU_TRAFFIC = {"gemv": 35_694_000, "gemm": 78_331_000 + 87_015_000}
 
 
 def algo_bytes(cfg) -> int:
-    """Algorithmic bytes per call: packed W + scales + x + y (SURVEY 8(d) figures)."""
+    """Algorithmic bytes per call: packed W + scales + x read once, y written once."""
     n, k, m = cfg["n"], cfg["k"], cfg["m"]
     bits = 6 if cfg["fmt"].startswith("fp6") else 4
     w = n * k * bits // 8
@@ -264,7 +268,7 @@ def run_gpu_arm(args, world, rank, local):
                                  "previous step drains; x read / y written only after it completes",
                        "parallelism": f"independent weights per GPU x{world}"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                         "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": NCU_TRAFFIC["gemv"],
                          "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)",
                          "algorithmic_bytes_per_launch": bytes_step},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
@@ -335,7 +339,7 @@ def run_gemm(args, device, world, rank):
         "config": {"workload": "c3 FP6 E3M2 packed GEMM M=4096 K=4096 N=14336, per-row fp16 scales, fp16 x/y",
                    "kernel": plan, "l2": "flushed (256 MB write) before each timed launch", "timed_launches": steps},
         "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": round(tflops / peaks["bf16_tflops"], 4), "traffic": None,
+                     "frac": round(tflops / peaks["bf16_tflops"], 4), "traffic": NCU_TRAFFIC["gemm"],
                      "peak_source": peaks["source"] + " (MEASURED_PEAKS.json bf16_tflops, dense fp16/bf16 kind)",
                      "algorithmic_flops_per_launch": flops},
     }
@@ -385,6 +389,33 @@ def cpu_baseline(nthreads: int, budget_s: float) -> dict:
                       f"{sec * 1e3:.1f} ms/call; oracle/cpu_ref.c decode-to-fp32 row + fp32 dot, OpenMP"}
 
 
+def profile_case(case: str, launches: int):
+    """Small untimed workload for ncu captures: `launches` plain b200_packed_linear calls.
+
+    gemv: c2 M=1 over 4 resident weight copies (143 MB > L2); gemm: c3 M=4096 (one weight).
+    Nothing is timed; the process only has to exit 0 so the same command line can be profiled.
+    """
+    import torch
+    from tinygrad_dx12_b200 import _lib
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    cfg = dict(GEMV_CFG if case == "gemv" else GEMM_CFG)
+    xdt = getattr(torch, cfg["xdt"])
+    ws = make_weights(cfg, device, 4 if case == "gemv" else 1, seed=0)
+    x = (torch.randn((cfg["m"], cfg["k"]), device=device) / 8).to(xdt)
+    y = torch.empty((cfg["m"], cfg["n"]), device=device, dtype=xdt)
+    code = _lib.DT[cfg["xdt"]]
+    fn = _lib.lib().b200_packed_linear
+    for i in range(launches):
+        d = ws[i % len(ws)].desc()
+        rc = fn(ctypes.byref(d), x.data_ptr(), code, cfg["m"], cfg["k"], 1, y.data_ptr(), code, cfg["n"], 1, 0, None)
+        if rc:
+            raise RuntimeError(_lib.last_error())
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": case, "launches": launches, "ok": True}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -394,7 +425,13 @@ def main():
     ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--profile-case", choices=["gemv", "gemm"], default=None,
+                    help="run a small untimed workload for ncu and exit")
+    ap.add_argument("--launches", type=int, default=6, help="launches of --profile-case")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case, args.launches)
+        return
     args.warmup = max(3, args.warmup)
     world, rank, local = dist_env()
     nthreads = os.cpu_count() or 1

@@ -338,7 +338,7 @@ def packed_linear_ref(spec: PackedSpec, x: np.ndarray, out_dtype: str | None = N
 
 
 # ----------------------------------------------------------------------------------
-# seeded synthetic inputs for BASELINE.json configs (test infrastructure)
+# seeded synthetic inputs for the benchmark configs c1..c5 (test infrastructure)
 # ----------------------------------------------------------------------------------
 E2M1_CODES = np.arange(16, dtype=np.uint8)
 E3M2_CODES = np.arange(64, dtype=np.uint8)  # all 64 are finite (-0 is code 32)

@@ -1,6 +1,6 @@
 """Fused packed linear (GEMV / tcgen05 GEMM / SIMT) against the float32 oracle.
 
-Shapes cover BASELINE.json's configs (c1 and c2 at full size; c3 at full K with fewer rows,
+Shapes cover the headline configs (c1 and c2 at full size; c3 at full K with fewer rows,
 plus a sampled-rows check at full size), odd tails, every format and scale dtype, and the
 three x / y dtypes. Tolerances: tests/helpers.py.
 """
@@ -62,7 +62,7 @@ PATHS = ["auto", "gemv", "simt", "gemm"]
 @pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("m", [1, 2, 3, 8, 17, 32])
 def test_c1_int4_gemv(path, m):
-    """BASELINE config 1 shape: INT4 4096x4096, per-32 fp16 scales, fp16 x and y."""
+    """Config c1 shape: INT4 4096x4096, per-32 fp16 scales, fp16 x and y."""
     spec = _spec("int4", 4096, 4096, 32, "f16u", 1)
     _run(spec, None, m, "float16", "float16", path)
 
@@ -71,7 +71,7 @@ def test_c1_int4_gemv(path, m):
 @pytest.mark.parametrize("m", [1, 8, 32])
 @pytest.mark.parametrize("scale", ["e8m0", "bfloat16"])
 def test_c2_fp4_gemv(path, m, scale):
-    """FP4 E2M1 8192x8192, per-32 2^e scales (E8M0 bytes or decoded bf16), bf16 x/y."""
+    """Config c2: FP4 E2M1 8192x8192, per-32 2^e scales (E8M0 bytes or decoded bf16), bf16 x/y."""
     spec = _spec("fp4_e2m1", 8192, 8192, 32, "e8m0", 2)
     _run(spec, scale, m, "bfloat16", "bfloat16", path)
 
@@ -79,7 +79,7 @@ def test_c2_fp4_gemv(path, m, scale):
 @pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("m", [64, 256, 300])
 def test_c3_fp6_gemm_reduced(path, m):
-    """BASELINE config 3 at full K=4096 with 1024 rows: FP6 E3M2, per-row fp16 scales, fp16 x (N(0,1)/8)."""
+    """Config c3 at full K=4096 with 1024 rows: FP6 E3M2, per-row fp16 scales, fp16 x (N(0,1)/8)."""
     spec = _spec("fp6_e3m2", 1024, 4096, 4096, "f16row", 3)
     _run(spec, None, m, "float16", "float16", path, xscale=0.125)
 

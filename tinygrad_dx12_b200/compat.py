@@ -2,15 +2,17 @@
 
 The reference's ``register()`` is idempotent, opens no hardware, injects its runtime module
 into ``sys.modules``, appends its device to tinygrad's ``Device._devices`` and puts it first in
-``ALL_DEVICES``. This module keeps those semantics for the device name ``B200`` when
-tinygrad is importable; without tinygrad (this image has none) registration only records
-that it happened, and the torch-tensor API in ``packed`` / ``linalg`` is the whole surface.
+``ALL_DEVICES``. Only the packed-matmul operators are rebuilt here; tinygrad's generic device
+runtime (allocator, queues, graph runner: ``runtime/ops_dx12.py``) is not. So ``register()``
+keeps the idempotent, hardware-free contract and records the registration, and the
+operator surface is ``PackedTensor`` / ``matmul`` / ``matvec`` over torch CUDA tensors
+(the tinygrad-side call into ``b200_packed_linear`` is the binding shown for maintainers
+next to the C header).
 """
 
 from __future__ import annotations
 
 import importlib
-import sys
 
 DEVICE = "B200"
 _registered = False
@@ -29,15 +31,6 @@ def register() -> None:
     global _registered
     if _registered:
         return
-    if tinygrad_available():
-        from tinygrad.device import ALL_DEVICES, Device  # noqa: WPS433 (optional dependency)
-
-        runtime = importlib.import_module("tinygrad_dx12_b200.runtime")
-        sys.modules["tinygrad.runtime.ops_b200"] = runtime
-        if DEVICE not in Device._devices:
-            Device._devices.append(DEVICE)
-        if DEVICE not in ALL_DEVICES:
-            ALL_DEVICES.insert(0, DEVICE)
     _registered = True
 
 

@@ -13,10 +13,10 @@
 //   warp 1 lane 0  MMA issuer: 4 x tcgen05.mma.kind::f16 (M=128, N=128, K=16) per stage into one
 //                  of two 128-column fp32 TMEM accumulators; tcgen05.commit frees the stage
 //                  (empty[s]) and, after the last stage of a tile, publishes the accumulator;
-//   warps 2..5     dequant warpgroup: each thread decodes one weight row of the stage (64
-//                  payloads) to exact fp16/bf16 (decode.cuh) and writes it in the 128-byte
-//                  swizzled K-major layout the MMA reads (bready[s]);
-//   warps 6..9     epilogue warpgroup: tcgen05.ld of the finished accumulator, per-column scale,
+//   warps 2..9     dequant warps (256 threads): each pair of threads decodes one weight row of
+//                  the stage (32 payloads each) to exact fp16/bf16 (decode.cuh) and writes it in
+//                  the 128-byte swizzled K-major layout the MMA reads (bready[s]);
+//   warps 10..13   epilogue warpgroup: tcgen05.ld of the finished accumulator, per-column scale,
 //                  cast, store; it frees the accumulator so the next-but-one tile can reuse it,
 //                  which overlaps each epilogue with the next tile's main loop.
 // Every mbarrier wait is bounded (sm100.cuh): on give-up the CTA drains its copies and MMAs,
