@@ -58,6 +58,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread may sleep in hardware (up to `hint_ns`) until
+// the phase completes instead of spinning through issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait that sleeps between polls (for warps with nothing else to do).
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, volatile uint32_t *abort_flag,
+                                                uint64_t budget_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > budget_ns) {
+      *abort_flag = 1;
+      atomicOr(&g_device_error, B200_DEVERR_MBAR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // Wait for phase `parity` of `bar`, giving up after `budget_ns` of wall time or as soon as
 // another thread of the CTA flagged an abort. Never traps; returns false on give-up.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort_flag,
