@@ -242,6 +242,9 @@ def run_gpu_arm(args, world, rank, local):
     gemm = None
     if not args.no_gemm:
         gemm = run_gemm(args, device, world, rank)
+    stack = None
+    if not args.no_stack:
+        stack = run_stack(args, device, world, rank)
     peaks = measured_peaks()
     result = None
     if rank == 0:
@@ -279,6 +282,8 @@ def run_gpu_arm(args, world, rank, local):
         }
         if gemm is not None:
             result["gemm"] = gemm
+        if stack is not None:
+            result["stack"] = stack
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -342,6 +347,67 @@ def run_gemm(args, device, world, rank):
                      "frac": round(tflops / peaks["bf16_tflops"], 4), "traffic": NCU_TRAFFIC["gemm"],
                      "peak_source": peaks["source"] + " (MEASURED_PEAKS.json bf16_tflops, dense fp16/bf16 kind)",
                      "algorithmic_flops_per_launch": flops},
+    }
+
+
+def run_stack(args, device, world, rank):
+    """c5 70B-shaped FP4 projection stack at M=1: one token through all layers per step,
+    tensor-parallel over the world (column-parallel q/k/v/gate/up, row-parallel o/down, two
+    fp32 NCCL all-reduces per layer). The whole forward is one CUDA graph."""
+    import torch
+    import torch.distributed as dist
+    from tinygrad_dx12_b200 import stack as S
+
+    cfg = S.C5
+    layers = cfg.layers if args.stack_layers is None else args.stack_layers
+    st = S.TPStack(cfg, rank, world, device=device, layers=layers, seed=11)
+    g = torch.Generator(device=device)
+    g.manual_seed(5)
+    h0 = torch.randn((1, cfg.hidden), device=device, generator=g).to(cfg.act)  # identical on every rank
+    h = h0.clone()
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for _ in range(2):  # eager warm-up (communicator set-up)
+            h.copy_(h0)
+            st.forward(h)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        h.copy_(h0)
+        st.forward(h)
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup // 4)):
+            graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    steps = max(3, min(args.steps, 20))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / steps], device=device)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    finite = bool(torch.isfinite(h.float()).all().item())
+    del graph  # holds NCCL work: released before the process group
+    torch.cuda.synchronize()
+    total = cfg.layer_weight_bytes() * layers
+    peaks = measured_peaks()
+    per_gpu = st.weight_bytes() / (ms / 1e3) / 1e9
+    return {
+        "workload": f"c5 70B-shaped FP4 E2M1 stack (per-32 E8M0), M=1 bf16, {layers} layers, tensor-parallel x{world}",
+        "ms_per_token": round(ms, 4), "tokens_per_s": round(1e3 / ms, 2),
+        "weight_bytes_per_token": total, "weight_gbs": round(total / (ms / 1e3) / 1e9, 1),
+        "per_gpu_weight_gbs": round(per_gpu, 1), "per_gpu_frac_of_hbm": round(per_gpu / peaks["hbm_gbs"], 4),
+        "allreduces_per_token": 2 * layers if world > 1 else 0, "kernels_per_token": layers * 8 + 1,
+        "timing": "CUDA graph of one forward (all layers + NCCL all-reduces), CUDA events, max over ranks",
+        "output_finite": finite,
     }
 
 
@@ -424,6 +490,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--no-stack", action="store_true", help="skip the c5 layer-stack leg")
+    ap.add_argument("--stack-layers", type=int, default=None, help="layers of the c5 stack leg (default: all 80)")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--profile-case", choices=["gemv", "gemm"], default=None,
                     help="run a small untimed workload for ncu and exit")

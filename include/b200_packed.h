@@ -172,6 +172,22 @@ int32_t b200_device_status(int32_t device, uint32_t *flags, int32_t clear);
 int32_t b200_device_wait_flag(const int32_t *flag, int32_t expect, int64_t max_spins, int32_t *status,
                               void *stream);
 
+/* ---- projection-stack glue (benchmark configs c4 / c5) --------------------------------
+ * No counterpart in the reference, whose packed path ends at one matmul
+ * (codegen/linalg.py:136-223); these are the elementwise steps between the packed
+ * projections of the multi-layer tensor-parallel stacks. Rows (tokens) are independent. */
+
+/* For each of the M rows of h (M x H, dtype h_dtype, row-major): if `partial` (fp32, M x H)
+ * is given, h += partial (fp32 add, rounded back to h_dtype in place); then, if `x` is given,
+ * x = h * rsqrt(mean(h^2) + eps) computed in fp32 and rounded to x_dtype. */
+int32_t b200_add_rmsnorm(void *h, int32_t h_dtype, const float *partial, void *x, int32_t x_dtype, int64_t M,
+                         int64_t H, float eps, void *stream);
+
+/* out[m, i] = gu[m, i] * gu[m, I + i] for gu (M x 2I) -- the gated product of a fused
+ * gate|up projection -- as an fp32 product rounded to out_dtype. */
+int32_t b200_gate_mul(const void *gu, int32_t gu_dtype, void *out, int32_t out_dtype, int64_t M, int64_t I,
+                      void *stream);
+
 #ifdef __cplusplus
 }
 #endif

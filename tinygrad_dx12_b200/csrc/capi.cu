@@ -290,6 +290,24 @@ int32_t b200_device_status(int32_t device, uint32_t *flags, int32_t clear) {
   return B200_OK;
 }
 
+int32_t b200_add_rmsnorm(void *h, int32_t h_dtype, const float *partial, void *x, int32_t x_dtype, int64_t M,
+                         int64_t H, float eps, void *stream) {
+  if (int32_t rc = injected()) return rc;
+  if (h == nullptr || M < 0 || H < 0) return b200_set_error(B200_ERR_INVALID, "bad add_rmsnorm arguments");
+  if (!dt_is_float(h_dtype) || (x != nullptr && !dt_is_float(x_dtype)))
+    return b200_set_error(B200_ERR_INVALID, "add_rmsnorm needs floating-point h / x");
+  return launch_add_rmsnorm(h, h_dtype, partial, x, x_dtype, M, H, eps, (cudaStream_t)stream);
+}
+
+int32_t b200_gate_mul(const void *gu, int32_t gu_dtype, void *out, int32_t out_dtype, int64_t M, int64_t I,
+                      void *stream) {
+  if (int32_t rc = injected()) return rc;
+  if (gu == nullptr || out == nullptr || M < 0 || I < 0) return b200_set_error(B200_ERR_INVALID, "bad gate_mul arguments");
+  if (!dt_is_float(gu_dtype) || !dt_is_float(out_dtype))
+    return b200_set_error(B200_ERR_INVALID, "gate_mul needs floating-point tensors");
+  return launch_gate_mul(gu, gu_dtype, out, out_dtype, M, I, (cudaStream_t)stream);
+}
+
 int32_t b200_device_wait_flag(const int32_t *flag, int32_t expect, int64_t max_spins, int32_t *status, void *stream) {
   if (flag == nullptr || status == nullptr) return b200_set_error(B200_ERR_INVALID, "null flag/status");
   if (max_spins < 0) return b200_set_error(B200_ERR_INVALID, "max_spins must be bounded");
