@@ -1,5 +1,5 @@
 // sm100.cuh -- thin inline-PTX wrappers for Blackwell (sm_100a): mbarriers with bounded waits,
-// TMA tensor loads (no multicast), tcgen05 TMEM allocation / MMA / commit / loads, and the
+// TMA tensor loads into this CTA only, tcgen05 TMEM allocation / MMA / commit / loads, and the
 // shared-memory matrix and instruction descriptors of tcgen05.mma kind::f16.
 //
 // Descriptor bit layouts follow the PTX ISA "tcgen05 matrix descriptors" section (the same
@@ -110,7 +110,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
 // Make generic-proxy shared-memory writes visible to the async proxy (TMA / tensor core).
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// 2-D TMA tile load into this CTA's shared memory, completion signalled on `bar` (no multicast).
+// 2-D TMA tile load into this CTA's shared memory, completion signalled on `bar` (this CTA only).
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int32_t x, int32_t y, uint64_t *bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
