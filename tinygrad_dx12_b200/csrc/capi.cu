@@ -133,7 +133,7 @@ static bool fill_linear(const b200_packed_desc *w, const void *x, int32_t x_dtyp
 static int32_t plan(const LinearArgs &a, bool kstride_ok, int32_t path) {
   if (!kstride_ok) return B200_ERR_UNSUPPORTED;
   path &= 0xFF;  // flag bits (B200_FLAG_*) do not select a kernel
-  const bool tc = gemv_tc_supported(a), gm = gemm_supported(a), simt = simt_supported(a);
+  const bool tc = gemv_tc_supported(a) || skinny_supported(a), gm = gemm_supported(a), simt = simt_supported(a);
   switch (path) {
     case B200_PATH_AUTO:
       if (a.m <= 32 && tc) return B200_PATH_GEMV;
@@ -169,7 +169,9 @@ int32_t b200_packed_linear(const b200_packed_desc *w, const void *x, int32_t x_d
   const int32_t p = plan(a, ks, path);
   cudaStream_t s = (cudaStream_t)stream;
   switch (p) {
-    case B200_PATH_GEMV: return gemv_stream_supported(a) ? launch_gemv_stream(a, s) : launch_gemv_tc(a, s);
+    case B200_PATH_GEMV:
+      if (a.m > 2) return launch_skinny(a, s);
+      return gemv_stream_supported(a) ? launch_gemv_stream(a, s) : launch_gemv_tc(a, s);
     case B200_PATH_GEMM: return launch_gemm(a, s);
     case B200_PATH_SIMT: return launch_gemv_simt(a, s);
   }
@@ -286,7 +288,9 @@ int32_t b200_device_status(int32_t device, uint32_t *flags, int32_t clear) {
   unsigned int v = 0, u = 0;
   if (int32_t rc = gemm_device_error(&v, clear != 0)) return rc;
   if (int32_t rc = gemv_device_error(&u, clear != 0)) return rc;
-  *flags = v | u;
+  unsigned int w = 0;
+  if (int32_t rc = skinny_device_error(&w, clear != 0)) return rc;
+  *flags = v | u | w;
   return B200_OK;
 }
 

@@ -325,6 +325,7 @@ static int scale_kind(const LinearArgs &a) {
 
 }  // namespace gemv
 
+#ifndef B200_GEMV_TC_NO_ENTRY  // the entry points are defined once (gemv.cu); other users take the helpers
 bool gemv_tc_supported(const LinearArgs &a) {
   using namespace gemv;
   if (a.m < 1 || a.m > 2) return false;
@@ -374,5 +375,7 @@ int32_t launch_gemv_tc(const LinearArgs &a, cudaStream_t stream) {
   }
   return b200_set_error(B200_ERR_INVALID, "unknown packed format %d", a.fmt);
 }
+
+#endif  // B200_GEMV_TC_NO_ENTRY
 
 }  // namespace b200

@@ -49,6 +49,11 @@ bool gemv_stream_supported(const LinearArgs &a);
 int32_t launch_gemv_stream(const LinearArgs &a, cudaStream_t stream);
 int32_t gemv_device_error(unsigned int *v, bool clear);
 
+// split-K mma.sync decode GEMM for 3 <= M <= 32, 4-bit formats (skinny.cu)
+bool skinny_supported(const LinearArgs &a);
+int32_t launch_skinny(const LinearArgs &a, cudaStream_t stream);
+int32_t skinny_device_error(unsigned int *v, bool clear);
+
 int32_t launch_matmul_generic(const void *a, int adt, int64_t sam, int64_t sak, const void *b, int bdt, int64_t sbk,
                               int64_t sbn, void *c, int cdt, int64_t scm, int64_t scn, int64_t M, int64_t N, int64_t K,
                               int accdt, cudaStream_t stream);

@@ -1,0 +1,606 @@
+// skinny.cu -- packed decode GEMM for a few tokens (3 <= M <= 32), 4-bit formats.
+//
+//   y[m, n] = sum_k x[m, k] * dequant(W)[n, k]
+//
+// The small-batch case of the reference's packed matmul (tinygrad-dx12
+// src/tinygrad_dx12/codegen/linalg.py:136-223 over dx12.py:69-106 decodes): too many tokens
+// for the M <= 2 streamed GEMV, too few for the tcgen05 GEMM, whose CUDA-core dequant costs
+// more instructions per weight than an HBM-bound pass can afford.
+//
+// One CTA owns 128 weight rows and one K slice (split-K keeps every SM busy when N is small):
+//   * warp 8, lane 0 streams per stage (512 K) the rows' packed codes (two 128-byte-swizzled
+//     TMA boxes), x[0:8*NT, stage] (eight 128-byte-swizzled boxes, rows past M zero-filled)
+//     and, for per-32 scales, the stage's scale tile into a shared-memory ring;
+//   * warps 0-7 consume: warp w owns rows 16w..16w+15. ldmatrix hands lane (g, t) payloads
+//     8t..8t+7 of one 32-payload block for rows g and g+8; the sm_100a conversions decode them
+//     to exact fp16; two mma.sync m16n8k16 per block and token tile give the block's partial
+//     sum for 8 tokens, scaled in fp32 by the block's scale (exact for every scale dtype).
+//     bf16 x is converted to fp16 in shared memory per stage with a per-token power-of-two
+//     prescale (max |x| of the chunk brought to [2^14, 2^15)), undone on the fp32 partials;
+//   * with one K slice the CTA stores y; otherwise it writes fp32 partials to a workspace,
+//     and the last CTA of the row block (atomic ticket) sums the slices in fixed order and
+//     stores y, then resets the ticket.
+// Every wait is bounded (sm100.cuh); on give-up the kernel flags the device error word.
+#include <map>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "sm100.cuh"
+#define B200_GEMV_TC_NO_ENTRY
+#include "gemv_tc.cuh"
+
+namespace b200 {
+
+int32_t skinny_device_error(unsigned int *v, bool clear) {
+  B200_CUDA_TRY(tu_device_error(v, clear));
+  return B200_OK;
+}
+
+namespace skinny {
+using namespace gemv;
+
+constexpr int CONSUMERS = 8, THREADS = (CONSUMERS + 1) * 32;
+constexpr int RB = 128;                 // weight rows per CTA (16 per consumer warp)
+constexpr int KST = 512;                // payloads per row per stage
+constexpr int W_BYTES = RB * KST / 2;   // 4-bit codes: 32 KB per stage
+template <int NT>
+__host__ __device__ constexpr int ctas_per_sm() {  // two resident CTAs while their rings fit
+  return NT <= 2 ? 2 : 1;
+}
+template <int NT>
+__host__ __device__ constexpr int smem_cap() {
+  return NT <= 2 ? 108 * 1024 : 210 * 1024;
+}
+
+template <int NT>
+__host__ __device__ constexpr int x_bytes() {  // 8 boxes of (8*NT tokens x 64 halves)
+  return 8 * (8 * NT) * 128;
+}
+__host__ __device__ constexpr int s_bytes(int esz) { return RB * (KST / 32) * esz; }
+template <int NT>
+__host__ __device__ constexpr int slot_bytes(int esz) {
+  return (W_BYTES + x_bytes<NT>() + s_bytes(esz) + 1023) / 1024 * 1024;
+}
+template <int NT>
+__host__ __device__ constexpr int stages(int esz) {
+  return smem_cap<NT>() / slot_bytes<NT>(esz) > 4   ? 4
+         : smem_cap<NT>() / slot_bytes<NT>(esz) < 2 ? 2
+                                                     : smem_cap<NT>() / slot_bytes<NT>(esz);
+}
+
+template <int SK>
+__host__ __device__ constexpr int tile_esz() {  // scale bytes staged per element (per-32 kinds)
+  return SK == SK_E8M0 ? 1 : SK == SK_F16 || SK == SK_BF16 ? 2 : SK == SK_F32 ? 4 : 0;
+}
+
+struct SkParams {
+  const void *scales;
+  int sdt;
+  int64_t nblk, block;
+  int block_log2;
+  const void *x;
+  int64_t m;
+  void *y;
+  int ydt;
+  int64_t ldy_m, ldy_n;
+  int64_t rows;
+  int nst;       // stages along K
+  int splits;    // K slices
+  int xbf16;
+  float *ws;     // [splits][m][rows] fp32 partials (splits > 1)
+  unsigned int *tickets;  // [row blocks]
+};
+
+// E8M0 byte -> 2^(b-127), branch-free (b = 0: 2^-127 subnormal; b = 255: NaN).
+__device__ __forceinline__ float e8m0_val(uint32_t b) {
+  const uint32_t bits = b == 0xFFu ? 0x7FC00000u : max(b << 23, 0x00400000u);
+  return __uint_as_float(bits);
+}
+
+template <int SK>
+__device__ __forceinline__ float tile_scale(const uint8_t *srow, int b) {
+  if constexpr (SK == SK_E8M0) return e8m0_val(srow[b]);
+  else if constexpr (SK == SK_F16) return __half2float(reinterpret_cast<const __half *>(srow)[b]);
+  else if constexpr (SK == SK_BF16) return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(srow)[b] << 16);
+  else if constexpr (SK == SK_F32) return reinterpret_cast<const float *>(srow)[b];
+  else return 1.f;
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t &d0, uint32_t &d1, uint32_t &d2, uint32_t &d3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CONSUMERS * 32) : "memory"); }
+
+// bf16 x chunk of the slot -> fp16 in place with a per-token power-of-two prescale; writes
+// the inverse factors to inv[8*NT]. Tokens are the box rows (8*NT per box, 8 boxes).
+template <int NT>
+__device__ __forceinline__ void convert_x(uint8_t *xs, float *inv, int tid) {
+  constexpr int TOK = 8 * NT, TPT = CONSUMERS * 32 / TOK;  // threads per token
+  const int tok = tid / TPT, part = tid % TPT;
+  // each token row holds 8 boxes x 8 chunks of 16 bytes = 64 chunks (positions are swizzled,
+  // which does not matter for an elementwise conversion)
+  float amax = 0.f;
+  for (int c = part; c < 64; c += TPT) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(xs + (c >> 3) * (TOK * 128) + tok * 128 + (c & 7) * 16);
+    const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(v[i] << 16)), fabsf(__uint_as_float(v[i] & 0xFFFF0000u))));
+  }
+#pragma unroll
+  for (int o = TPT / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  // prescale 2^(14 - e) with e the exponent of amax (amax = 0: factor 1)
+  int e = amax > 0.f ? ((__float_as_int(amax) >> 23) & 0xFF) - 127 : 14;
+  e = e > 126 ? 126 : (e < -112 ? -112 : e);  // both factors stay normal floats
+  const float ps = __int_as_float((127 + 14 - e) << 23);
+  if (part == 0) inv[tok] = __int_as_float((127 - 14 + e) << 23);
+  for (int c = part; c < 64; c += TPT) {
+    uint4 *p = reinterpret_cast<uint4 *>(xs + (c >> 3) * (TOK * 128) + tok * 128 + (c & 7) * 16);
+    const uint4 u = *p;
+    const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 h = __floats2half2_rn(__uint_as_float(v[i] << 16) * ps, __uint_as_float(v[i] & 0xFFFF0000u) * ps);
+      o[i] = *reinterpret_cast<const uint32_t *>(&h);
+    }
+    *p = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+template <int FMT, int NT, int SK, bool XBF16>
+__global__ void __launch_bounds__(THREADS, ctas_per_sm<NT>())
+    skinny_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
+                  const __grid_constant__ CUtensorMap tms, SkParams p) {
+  constexpr int ESZ = tile_esz<SK>();
+  constexpr bool TILE_SCALES = ESZ > 0;
+  constexpr int SLOT = slot_bytes<NT>(ESZ);
+  constexpr int STAGES = stages<NT>(ESZ);
+  constexpr int TOK = 8 * NT;
+  constexpr uint32_t TX = W_BYTES + x_bytes<NT>() + (TILE_SCALES ? s_bytes(ESZ) : 0);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *ring = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t *full = reinterpret_cast<uint64_t *>(ring + STAGES * SLOT);
+  uint64_t *empty = full + STAGES;
+  volatile uint32_t *abort_flag = reinterpret_cast<uint32_t *>(empty + STAGES);
+  volatile uint32_t *last_flag = abort_flag + 1;
+  float *inv = const_cast<float *>(reinterpret_cast<volatile float *>(abort_flag + 2));  // [STAGES][TOK]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rblk = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
+  const int st0 = (int)((int64_t)p.nst * split / p.splits), st1 = (int)((int64_t)p.nst * (split + 1) / p.splits);
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], CONSUMERS);
+    }
+    *abort_flag = 0;
+    *last_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == CONSUMERS) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      prefetch_tmap(&tmw);
+      prefetch_tmap(&tmx);
+      if constexpr (TILE_SCALES) prefetch_tmap(&tms);
+      int slot = 0, issued = 0;
+      uint32_t ph = 0;
+      for (int st = st0; st < st1; ++st) {
+        if (issued >= STAGES && !mbar_wait(&empty[slot], ph ^ 1u, abort_flag)) break;
+        if (*abort_flag) break;
+        uint8_t *dst = ring + slot * SLOT;
+        mbar_arrive_expect_tx(&full[slot], TX);
+        tma_load_2d(dst, &tmw, st * (KST / 2), rblk * RB, &full[slot]);
+        tma_load_2d(dst + RB * 128, &tmw, st * (KST / 2) + 128, rblk * RB, &full[slot]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) tma_load_2d(dst + W_BYTES + j * (TOK * 128), &tmx, st * KST + 64 * j, 0, &full[slot]);
+        if constexpr (TILE_SCALES)
+          tma_load_2d(dst + W_BYTES + x_bytes<NT>(), &tms, st * (KST / 32), rblk * RB, &full[slot]);
+        ++issued;
+        if (++slot == STAGES) slot = 0, ph ^= 1u;
+      }
+      if (*abort_flag) {  // drain copies still in flight before exiting
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          int s = slot - 1 - i;
+          uint32_t q = ph;
+          if (s < 0) s += STAGES, q ^= 1u;
+          mbar_wait(&full[s], q, abort_flag, 200000000ull);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int g = lane >> 2, t = lane & 3;
+  const int r0 = warp * 16;  // this warp's rows r0 + g, r0 + g + 8 (within the CTA's 128)
+  const int64_t nlo = (int64_t)rblk * RB + r0 + g, nhi = nlo + 8;
+  float acc[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  // ldmatrix row address for this lane: matrix q = lane / 8 (rows +0/+8, chunk +0/+1), row i
+  const int lq = lane >> 3, li = lane & 7;
+  const int lrow = r0 + (lq & 1) * 8 + li;
+  const int lchunk = lq >> 1;
+  // x fragment offsets within a box: token row g, 16-byte chunk t (even block) / 4 + t (odd)
+  const int xoff[2] = {g * 128 + ((t ^ g) << 4), g * 128 + (((4 + t) ^ g) << 4)};
+
+  int slot = 0;
+  uint32_t ph = 0;
+  for (int st = st0; st < st1; ++st) {
+    // SK_GROUP: the scales of the groups that end in this stage, indexed by their last block
+    // (prefetched before the stage wait; compile-time indices keep them in registers)
+    float sgl[KST / 32], sgh[KST / 32];
+    if constexpr (SK == SK_GROUP) {
+#pragma unroll
+      for (int bb = 0; bb < KST / 32; ++bb) {
+        sgl[bb] = sgh[bb] = 0.f;
+        if (((32 * (bb + 1)) & (p.block - 1)) == 0) {
+          const int64_t gi = ((int64_t)st * KST + 32 * bb) >> p.block_log2;
+          if (nlo < p.rows) sgl[bb] = load_as_f32(p.scales, nlo * p.nblk + gi, p.sdt);
+          if (nhi < p.rows) sgh[bb] = load_as_f32(p.scales, nhi * p.nblk + gi, p.sdt);
+        }
+      }
+    }
+    const bool got = mbar_wait(&full[slot], ph, abort_flag);
+    uint8_t *base = ring + slot * SLOT;
+    uint8_t *xs = base + W_BYTES;
+    float *sinv = inv + slot * TOK;
+    if constexpr (XBF16) {
+      if (got) convert_x<NT>(xs, sinv, tid);
+      consumer_sync();
+    }
+    float sacc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+    if (got) {
+      const uint8_t *srow_lo = base + W_BYTES + x_bytes<NT>() + (r0 + g) * (KST / 32) * ESZ;
+      const uint8_t *srow_hi = srow_lo + 8 * (KST / 32) * ESZ;
+      const uint32_t wbase = smem_u32(base);
+      uint4 e8lo = make_uint4(0u, 0u, 0u, 0u), e8hi = e8lo;  // the stage's 16 E8M0 scales of rows g / g+8
+      bool e8fast = false;
+      if constexpr (SK == SK_E8M0) {
+        e8lo = *reinterpret_cast<const uint4 *>(srow_lo);
+        e8hi = *reinterpret_cast<const uint4 *>(srow_hi);
+        // a normal fp16 2^e with e in [-14, 12] multiplies every decoded 4-bit payload exactly
+        // (at most two significant bits, 0.5 <= |value| <= 8: products stay within fp16, down to
+        // its subnormal quantum 2^-24): E8M0 bytes 113..139
+        const uint32_t wv[8] = {e8lo.x, e8lo.y, e8lo.z, e8lo.w, e8hi.x, e8hi.y, e8hi.z, e8hi.w};
+        uint32_t inr = 0xFFFFFFFFu;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) inr &= __vcmpgeu4(wv[i], 0x71717171u) & __vcmpleu4(wv[i], 0x8B8B8B8Bu);
+        e8fast = __all_sync(0xffffffffu, inr == 0xFFFFFFFFu);
+      }
+      float gd[NT][4];  // running partial of the current scale group (SK_GROUP)
+#pragma unroll
+      for (int j = 0; j < NT; ++j) gd[j][0] = gd[j][1] = gd[j][2] = gd[j][3] = 0.f;
+#pragma unroll
+      for (int bp = 0; bp < KST / 64; ++bp) {  // pairs of 32-payload blocks
+        const int b = 2 * bp;
+        const int box = b >> 3, chunk = (b & 7) + lchunk;
+        uint32_t wl0, wh0, wl1, wh1;  // rows g / g+8 of blocks b / b+1
+        ldmatrix_x4(wbase + box * (RB * 128) + lrow * 128 + (((chunk) ^ (lrow & 7)) << 4), wl0, wh0, wl1, wh1);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int bb = b + h;
+          uint32_t ol[4], oh[4];
+          const uint32_t wl = h ? wl1 : wl0, wh = h ? wh1 : wh0;
+          decode8_natural<FMT, false>(&wl, 0, ol);
+          decode8_natural<FMT, false>(&wh, 0, oh);
+          const int xbox = bb >> 1;
+          float sl = 1.f, sh = 1.f;
+          if constexpr (SK == SK_E8M0) {
+            const uint32_t wlo = bb < 4 ? e8lo.x : bb < 8 ? e8lo.y : bb < 12 ? e8lo.z : e8lo.w;
+            const uint32_t whi = bb < 4 ? e8hi.x : bb < 8 ? e8hi.y : bb < 12 ? e8hi.z : e8hi.w;
+            const uint32_t bl = (wlo >> (8 * (bb & 3))) & 0xFFu, bh = (whi >> (8 * (bb & 3))) & 0xFFu;
+            if (e8fast) {  // fp16 2^(b-127) = bits (b - 112) << 10, exact in range; both halves
+              const uint32_t hl = (bl - 112u) << 10, hh = (bh - 112u) << 10;
+              const __half2 s2l = __halves2half2(__ushort_as_half((unsigned short)hl), __ushort_as_half((unsigned short)hl));
+              const __half2 s2h = __halves2half2(__ushort_as_half((unsigned short)hh), __ushort_as_half((unsigned short)hh));
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const __half2 vl = __hmul2(*reinterpret_cast<const __half2 *>(&ol[i]), s2l);
+                const __half2 vh = __hmul2(*reinterpret_cast<const __half2 *>(&oh[i]), s2h);
+                ol[i] = *reinterpret_cast<const uint32_t *>(&vl);
+                oh[i] = *reinterpret_cast<const uint32_t *>(&vh);
+              }
+            } else {
+              sl = e8m0_val(bl);
+              sh = e8m0_val(bh);
+            }
+          } else if constexpr (TILE_SCALES) {
+            sl = tile_scale<SK>(srow_lo, bb);
+            sh = tile_scale<SK>(srow_hi, bb);
+          }
+          const uint32_t a0[4] = {ol[0], oh[0], ol[1], oh[1]}, a1[4] = {ol[2], oh[2], ol[3], oh[3]};
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            const uint4 xv = *reinterpret_cast<const uint4 *>(xs + xbox * (TOK * 128) + (8 * j) * 128 + xoff[bb & 1]);
+            if (SK == SK_E8M0 && e8fast) {
+              mma16816(sacc[j], a0, xv.x, xv.y);
+              mma16816(sacc[j], a1, xv.z, xv.w);
+            } else if constexpr (TILE_SCALES) {
+              float d[4] = {0.f, 0.f, 0.f, 0.f};
+              mma16816(d, a0, xv.x, xv.y);
+              mma16816(d, a1, xv.z, xv.w);
+              sacc[j][0] = fmaf(d[0], sl, sacc[j][0]);
+              sacc[j][1] = fmaf(d[1], sl, sacc[j][1]);
+              sacc[j][2] = fmaf(d[2], sh, sacc[j][2]);
+              sacc[j][3] = fmaf(d[3], sh, sacc[j][3]);
+            } else if constexpr (SK == SK_GROUP) {
+              mma16816(gd[j], a0, xv.x, xv.y);
+              mma16816(gd[j], a1, xv.z, xv.w);
+            } else {
+              mma16816(sacc[j], a0, xv.x, xv.y);
+              mma16816(sacc[j], a1, xv.z, xv.w);
+            }
+          }
+          if constexpr (SK == SK_GROUP) {
+            if (((32 * (bb + 1)) & (p.block - 1)) == 0) {  // the group ends with this block
+              const float gl = sgl[bb], gh = sgh[bb];
+#pragma unroll
+              for (int j = 0; j < NT; ++j) {
+                sacc[j][0] = fmaf(gd[j][0], gl, sacc[j][0]);
+                sacc[j][1] = fmaf(gd[j][1], gl, sacc[j][1]);
+                sacc[j][2] = fmaf(gd[j][2], gh, sacc[j][2]);
+                sacc[j][3] = fmaf(gd[j][3], gh, sacc[j][3]);
+                gd[j][0] = gd[j][1] = gd[j][2] = gd[j][3] = 0.f;
+              }
+            }
+          }
+        }
+      }
+    }
+    // the slot's bytes are no longer needed (generic-proxy writes ordered before the next TMA fill)
+    if constexpr (XBF16) fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const float f0 = XBF16 ? sinv[8 * j + 2 * t] : 1.f, f1 = XBF16 ? sinv[8 * j + 2 * t + 1] : 1.f;
+      acc[j][0] = fmaf(sacc[j][0], f0, acc[j][0]);
+      acc[j][1] = fmaf(sacc[j][1], f1, acc[j][1]);
+      acc[j][2] = fmaf(sacc[j][2], f0, acc[j][2]);
+      acc[j][3] = fmaf(sacc[j][3], f1, acc[j][3]);
+    }
+    if (++slot == STAGES) slot = 0, ph ^= 1u;
+  }
+
+  // ---------------- epilogue ----------------
+  const bool ok = !*abort_flag;
+  float rs_lo = 1.f, rs_hi = 1.f;
+  if constexpr (SK == SK_ROW) {
+    if (nlo < p.rows) rs_lo = load_as_f32(p.scales, nlo * p.nblk, p.sdt);
+    if (nhi < p.rows) rs_hi = load_as_f32(p.scales, nhi * p.nblk, p.sdt);
+  }
+  if (p.splits == 1) {
+    if (!ok) return;
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t m = 8 * j + 2 * t + (i & 1), n = i < 2 ? nlo : nhi;
+        if (m < p.m && n < p.rows) store_f32(p.y, m * p.ldy_m + n * p.ldy_n, p.ydt, acc[j][i] * (i < 2 ? rs_lo : rs_hi));
+      }
+    return;
+  }
+  // split-K: partials to the workspace, then the last CTA of the row block reduces
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t m = 8 * j + 2 * t + (i & 1), n = i < 2 ? nlo : nhi;
+      if (m < p.m && n < p.rows) p.ws[((int64_t)split * p.m + m) * p.rows + n] = acc[j][i];
+    }
+  __threadfence();
+  consumer_sync();
+  if (tid == 0) {
+    const unsigned int ticket = atomicAdd(&p.tickets[rblk], 1u);
+    *last_flag = ticket == (unsigned int)(p.splits - 1);
+  }
+  consumer_sync();
+  if (!*last_flag) return;
+  __threadfence();
+  const int64_t n0 = (int64_t)rblk * RB;
+  for (int e = tid; e < RB * (int)p.m; e += CONSUMERS * 32) {
+    const int64_t m = e / RB, n = n0 + e % RB;
+    if (n >= p.rows) continue;
+    float s = 0.f;
+    for (int sp = 0; sp < p.splits; ++sp) s += __ldcg(&p.ws[((int64_t)sp * p.m + m) * p.rows + n]);
+    if constexpr (SK == SK_ROW) s *= load_as_f32(p.scales, n * p.nblk, p.sdt);
+    if (ok) store_f32(p.y, m * p.ldy_m + n * p.ldy_n, p.ydt, s);
+  }
+  if (tid == 0) p.tickets[rblk] = 0u;  // ready for the next call on this workspace
+}
+
+template <int NT>
+static size_t smem_bytes(int esz) {
+  return 1024 + (size_t)stages<NT>(esz) * slot_bytes<NT>(esz) + 2 * 4 * 8 + 16 + 4 * 8 * NT * 4;
+}
+
+// ---- per-(device, stream) split-K workspace --------------------------------------------------
+struct Workspace {
+  float *ws = nullptr;
+  unsigned int *tickets = nullptr;
+  size_t ws_bytes = 0, tickets_n = 0;
+};
+constexpr size_t WS_BYTES = 16u << 20;  // fp32 partials (max splits x M x N)
+constexpr size_t TICKETS = 16384;       // row blocks (N up to 2M rows)
+
+static std::mutex g_ws_mutex;
+static std::map<std::pair<int, cudaStream_t>, Workspace> g_ws;
+
+static int32_t workspace_for(cudaStream_t stream, Workspace *&out) {
+  int dev = 0;
+  B200_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  auto it = g_ws.find({dev, stream});
+  if (it != g_ws.end()) {
+    out = &it->second;
+    return B200_OK;
+  }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  B200_CUDA_TRY(cudaStreamIsCapturing(stream, &cs));
+  if (cs != cudaStreamCaptureStatusNone) {  // no allocation while capturing: run unsplit
+    out = nullptr;
+    return B200_OK;
+  }
+  Workspace w;
+  B200_CUDA_TRY(cudaMalloc((void **)&w.ws, WS_BYTES));
+  B200_CUDA_TRY(cudaMalloc((void **)&w.tickets, TICKETS * sizeof(unsigned int)));
+  B200_CUDA_TRY(cudaMemset(w.tickets, 0, TICKETS * sizeof(unsigned int)));
+  w.ws_bytes = WS_BYTES;
+  w.tickets_n = TICKETS;
+  out = &(g_ws[{dev, stream}] = w);
+  return B200_OK;
+}
+
+template <int FMT, int NT, int SK, bool XBF16>
+static int32_t launch_t(const LinearArgs &a, int splits, float *ws, unsigned int *tickets, cudaStream_t stream) {
+  constexpr int ESZ = tile_esz<SK>();
+  static bool attr = false;
+  const size_t smem = smem_bytes<NT>(ESZ);
+  if (!attr) {
+    B200_CUDA_TRY(cudaFuncSetAttribute(skinny_kernel<FMT, NT, SK, XBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem));
+    attr = true;
+  }
+  CUtensorMap tmw, tmx, tms;
+  const uint64_t row_bytes = (uint64_t)a.cols / 2;
+  if (int32_t rc = make_tma_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, row_bytes, (uint64_t)a.rows, row_bytes, 128,
+                               RB, CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  if (int32_t rc = make_tma_2d(&tmx, XBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x,
+                               (uint64_t)a.cols, (uint64_t)a.m, (uint64_t)a.ldx * 2, 64, 8 * NT,
+                               CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  if constexpr (ESZ > 0) {
+    const CUtensorMapDataType dt = ESZ == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : ESZ == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : SK == SK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if (int32_t rc = make_tma_2d(&tms, dt, a.scales, (uint64_t)a.nblk, (uint64_t)a.rows, (uint64_t)a.nblk * ESZ,
+                                 KST / 32, RB, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+  } else {
+    tms = tmw;
+  }
+  SkParams p;
+  p.scales = a.scales, p.sdt = a.sdt, p.nblk = a.nblk, p.block = a.block;
+  p.block_log2 = 0;
+  while (((int64_t)1 << p.block_log2) < a.block) ++p.block_log2;
+  p.x = a.x, p.m = a.m, p.y = a.y, p.ydt = a.ydt, p.ldy_m = a.ldy_m, p.ldy_n = a.ldy_n, p.rows = a.rows;
+  p.nst = (int)(a.cols / KST);
+  p.splits = splits;
+  p.xbf16 = XBF16;
+  p.ws = ws;
+  p.tickets = tickets;
+  const int64_t nrb = (a.rows + RB - 1) / RB;
+  skinny_kernel<FMT, NT, SK, XBF16><<<(unsigned)(nrb * splits), THREADS, smem, stream>>>(tmw, tmx, tms, p);
+  B200_LAUNCH_CHECK();
+  return B200_OK;
+}
+
+template <int FMT, int NT, int SK>
+static int32_t launch_x(const LinearArgs &a, int splits, float *ws, unsigned int *tk, cudaStream_t s) {
+  return a.xdt == B200_DT_BF16 ? launch_t<FMT, NT, SK, true>(a, splits, ws, tk, s)
+                               : launch_t<FMT, NT, SK, false>(a, splits, ws, tk, s);
+}
+
+template <int FMT, int NT>
+static int32_t launch_sk(const LinearArgs &a, int sk, int splits, float *ws, unsigned int *tk, cudaStream_t s) {
+  switch (sk) {
+    case SK_NONE: return launch_x<FMT, NT, SK_NONE>(a, splits, ws, tk, s);
+    case SK_ROW: return launch_x<FMT, NT, SK_ROW>(a, splits, ws, tk, s);
+    case SK_E8M0: return launch_x<FMT, NT, SK_E8M0>(a, splits, ws, tk, s);
+    case SK_F16: return launch_x<FMT, NT, SK_F16>(a, splits, ws, tk, s);
+    case SK_BF16: return launch_x<FMT, NT, SK_BF16>(a, splits, ws, tk, s);
+    case SK_F32: return launch_x<FMT, NT, SK_F32>(a, splits, ws, tk, s);
+    case SK_GROUP: return launch_x<FMT, NT, SK_GROUP>(a, splits, ws, tk, s);
+  }
+  return b200_set_error(B200_ERR_UNSUPPORTED, "skinny GEMM: scale layout");
+}
+
+template <int FMT>
+static int32_t launch_nt(const LinearArgs &a, int sk, int splits, float *ws, unsigned int *tk, cudaStream_t s) {
+  if (a.m <= 8) return launch_sk<FMT, 1>(a, sk, splits, ws, tk, s);
+  if (a.m <= 16) return launch_sk<FMT, 2>(a, sk, splits, ws, tk, s);
+  return launch_sk<FMT, 4>(a, sk, splits, ws, tk, s);
+}
+
+static int choose_splits(const LinearArgs &a, int sms) {
+  const int64_t nrb = (a.rows + RB - 1) / RB, nst = a.cols / KST;
+  int64_t s = sms / nrb;
+  if (s < 1) s = 1;
+  if (s > nst) s = nst;
+  if (s > 16) s = 16;
+  return (int)s;
+}
+
+}  // namespace skinny
+
+bool skinny_supported(const LinearArgs &a) {
+  using namespace skinny;
+  if (a.m < 3 || a.m > 32) return false;
+  if (!(a.fmt == B200_FMT_INT4 || a.fmt == B200_FMT_UINT4 || a.fmt == B200_FMT_FP4_E2M1)) return false;
+  if (a.xdt != B200_DT_F16 && a.xdt != B200_DT_BF16) return false;
+  if (a.ydt != B200_DT_F16 && a.ydt != B200_DT_BF16 && a.ydt != B200_DT_F32) return false;
+  if (a.cols < KST || a.cols % KST != 0 || a.cols > ((int64_t)1 << 26) || a.rows <= 0) return false;
+  if ((a.rows + RB - 1) / RB * 16 > (int64_t)INT32_MAX) return false;
+  if ((uintptr_t)a.w % 16 != 0 || (uintptr_t)a.x % 16 != 0 || (a.ldx * 2) % 16 != 0) return false;
+  if (a.scales != nullptr) {
+    const int sk = gemv::scale_kind(a);
+    if (sk == gemv::SK_GROUP) {
+      if (!(a.block == 64 || a.block == 128 || a.block == 256 || a.block == 512)) return false;
+      if (!(a.sdt == B200_DT_F16 || a.sdt == B200_DT_BF16 || a.sdt == B200_DT_F32 || a.sdt == B200_DT_E8M0)) return false;
+    } else if (sk >= gemv::SK_E8M0) {
+      if ((a.nblk * dt_size(a.sdt)) % 16 != 0 || (uintptr_t)a.scales % 16 != 0) return false;
+    } else if (sk == gemv::SK_ROW) {
+      if (!(a.sdt == B200_DT_F16 || a.sdt == B200_DT_BF16 || a.sdt == B200_DT_F32 || a.sdt == B200_DT_E8M0)) return false;
+    }
+  }
+  return true;
+}
+
+int32_t launch_skinny(const LinearArgs &a, cudaStream_t stream) {
+  using namespace skinny;
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    B200_CUDA_TRY(cudaGetDevice(&dev));
+    B200_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  int splits = choose_splits(a, sms * (a.m <= 16 ? 2 : 1));
+  float *ws = nullptr;
+  unsigned int *tickets = nullptr;
+  if (splits > 1) {
+    Workspace *w = nullptr;
+    if (int32_t rc = workspace_for(stream, w)) return rc;
+    const int64_t nrb = (a.rows + RB - 1) / RB;
+    const size_t per_split = (size_t)a.m * a.rows * sizeof(float);
+    if (w == nullptr || (size_t)nrb > w->tickets_n) {
+      splits = 1;
+    } else {
+      while (splits > 1 && (size_t)splits * per_split > w->ws_bytes) --splits;
+      ws = w->ws;
+      tickets = w->tickets;
+    }
+  }
+  const int sk = gemv::scale_kind(a);
+  switch (a.fmt) {
+    case B200_FMT_INT4: return launch_nt<B200_FMT_INT4>(a, sk, splits, ws, tickets, stream);
+    case B200_FMT_UINT4: return launch_nt<B200_FMT_UINT4>(a, sk, splits, ws, tickets, stream);
+    case B200_FMT_FP4_E2M1: return launch_nt<B200_FMT_FP4_E2M1>(a, sk, splits, ws, tickets, stream);
+  }
+  return b200_set_error(B200_ERR_UNSUPPORTED, "skinny GEMM: format %d", a.fmt);
+}
+
+}  // namespace b200
