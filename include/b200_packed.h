@@ -172,6 +172,19 @@ int32_t b200_device_status(int32_t device, uint32_t *flags, int32_t clear);
 int32_t b200_device_wait_flag(const int32_t *flag, int32_t expect, int64_t max_spins, int32_t *status,
                               void *stream);
 
+/* Allocation-free form of b200_packed_linear for a few tokens (3 <= m <= 32, 4-bit formats,
+ * the split-K decode GEMM). No counterpart in the reference. Same arguments and result as
+ * b200_packed_linear with path B200_PATH_GEMV and unit k / n strides; bitwise the same result.
+ * It never allocates device memory: its split-K scratch is a fixed 2 MiB device array of the
+ * library (per device), resolved on the first call on a device -- make that first call before
+ * any stream capture. Shapes whose split-K partials would not fit (splits x m x N x 4 bytes
+ * beyond the 2 MiB less 16 KiB of row-block tickets, or more than 4096 row blocks of 128
+ * rows) return B200_ERR_UNSUPPORTED; shapes the kernel does not take return the same error.
+ * Calls that overlap in time on one device (several streams or threads) share the array and
+ * race: serialise them. */
+int32_t b200_packed_linear_noalloc(const b200_packed_desc *w, const void *x, int32_t x_dtype, int64_t m,
+                                   int64_t x_stride_m, void *y, int32_t y_dtype, int64_t y_stride_m, void *stream);
+
 /* ---- projection-stack glue (benchmark configs c4 / c5) --------------------------------
  * No counterpart in the reference, whose packed path ends at one matmul
  * (codegen/linalg.py:136-223); these are the elementwise steps between the packed

@@ -294,6 +294,23 @@ int32_t b200_device_status(int32_t device, uint32_t *flags, int32_t clear) {
   return B200_OK;
 }
 
+int32_t b200_packed_linear_noalloc(const b200_packed_desc *w, const void *x, int32_t x_dtype, int64_t m,
+                                   int64_t x_stride_m, void *y, int32_t y_dtype, int64_t y_stride_m, void *stream) {
+  if (int32_t rc = injected()) return rc;
+  if (int32_t rc = validate_desc(w)) return rc;
+  if (m < 0) return b200_set_error(B200_ERR_INVALID, "negative m");
+  if (m == 0 || w->rows == 0) return B200_OK;
+  if (x == nullptr || y == nullptr) return b200_set_error(B200_ERR_INVALID, "null x or y");
+  LinearArgs a;
+  fill_linear(w, x, x_dtype, m, x_stride_m, 1, y, y_dtype, y_stride_m, 1, a);
+  if (m < 3 || !skinny_supported(a))
+    return b200_set_error(B200_ERR_UNSUPPORTED,
+                          "packed_linear_noalloc: no split-K decode GEMM for format=%d scale_dtype=%d block=%lld "
+                          "K=%lld x_dtype=%d y_dtype=%d m=%lld",
+                          a.fmt, a.sdt, (long long)a.block, (long long)a.cols, a.xdt, a.ydt, (long long)m);
+  return launch_skinny_noalloc(a, (cudaStream_t)stream);
+}
+
 int32_t b200_add_rmsnorm(void *h, int32_t h_dtype, const float *partial, void *x, int32_t x_dtype, int64_t M,
                          int64_t H, float eps, void *stream) {
   if (int32_t rc = injected()) return rc;

@@ -53,6 +53,8 @@ int32_t gemv_device_error(unsigned int *v, bool clear);
 bool skinny_supported(const LinearArgs &a);
 int32_t launch_skinny(const LinearArgs &a, cudaStream_t stream);
 int32_t skinny_device_error(unsigned int *v, bool clear);
+// same kernel, split-K scratch from a fixed device array instead of a library workspace
+int32_t launch_skinny_noalloc(const LinearArgs &a, cudaStream_t stream);
 
 int32_t launch_matmul_generic(const void *a, int adt, int64_t sam, int64_t sak, const void *b, int bdt, int64_t sbk,
                               int64_t sbn, void *c, int cdt, int64_t scm, int64_t scn, int64_t M, int64_t N, int64_t K,

@@ -604,3 +604,74 @@ int32_t launch_skinny(const LinearArgs &a, cudaStream_t stream) {
 }
 
 }  // namespace b200
+
+// ---- allocation-free variant (b200_packed_linear_noalloc) ---------------------------------
+// The split-K scratch (row-block tickets, then fp32 partials) lives in one fixed device array
+// of this translation unit; nothing is allocated. The tickets must start at zero: the array is
+// zero-initialised when the module loads, setup clears them once more, and every reducing CTA
+// resets its ticket. Calls that overlap in time on one device share the array and race.
+namespace b200 {
+namespace skinny {
+
+constexpr size_t NOALLOC_SCRATCH_BYTES = 2u << 20;  // 2 MiB per device
+constexpr size_t NOALLOC_TICKETS = 4096;            // row blocks of 128 rows (N <= 524288)
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+static std::mutex g_noalloc_mutex;
+static std::map<int, unsigned char *> g_noalloc_base;  // device -> address of the array
+
+// Resolve the array's device address once per device (and clear the tickets).
+static int32_t noalloc_scratch(unsigned char *&base) {
+  int dev = 0;
+  B200_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  auto it = g_noalloc_base.find(dev);
+  if (it != g_noalloc_base.end()) {
+    base = it->second;
+    return B200_OK;
+  }
+  void *p = nullptr;
+  B200_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+  B200_CUDA_TRY(cudaMemset(p, 0, NOALLOC_TICKETS * sizeof(unsigned int)));
+  base = static_cast<unsigned char *>(p);
+  g_noalloc_base[dev] = base;
+  return B200_OK;
+}
+
+}  // namespace skinny
+
+int32_t launch_skinny_noalloc(const LinearArgs &a, cudaStream_t stream) {
+  using namespace skinny;
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    B200_CUDA_TRY(cudaGetDevice(&dev));
+    B200_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  const int splits = choose_splits(a, sms * (a.m <= 16 ? 2 : 1));  // as b200_packed_linear
+  float *ws = nullptr;
+  unsigned int *tickets = nullptr;
+  if (splits > 1) {
+    const int64_t nrb = (a.rows + RB - 1) / RB;
+    const size_t tbytes = NOALLOC_TICKETS * sizeof(unsigned int);
+    const size_t need = (size_t)splits * a.m * a.rows * sizeof(float);
+    if ((size_t)nrb > NOALLOC_TICKETS || need > NOALLOC_SCRATCH_BYTES - tbytes)
+      return b200_set_error(B200_ERR_UNSUPPORTED,
+                            "packed_linear_noalloc: needs %zu bytes of split-K scratch for %lld row blocks; the "
+                            "fixed scratch holds %zu bytes and %zu row blocks",
+                            need, (long long)nrb, NOALLOC_SCRATCH_BYTES - tbytes, NOALLOC_TICKETS);
+    unsigned char *base = nullptr;
+    if (int32_t rc = noalloc_scratch(base)) return rc;
+    tickets = reinterpret_cast<unsigned int *>(base);
+    ws = reinterpret_cast<float *>(base + tbytes);
+  }
+  const int sk = gemv::scale_kind(a);
+  switch (a.fmt) {
+    case B200_FMT_INT4: return launch_nt<B200_FMT_INT4>(a, sk, splits, ws, tickets, stream);
+    case B200_FMT_UINT4: return launch_nt<B200_FMT_UINT4>(a, sk, splits, ws, tickets, stream);
+    case B200_FMT_FP4_E2M1: return launch_nt<B200_FMT_FP4_E2M1>(a, sk, splits, ws, tickets, stream);
+  }
+  return b200_set_error(B200_ERR_UNSUPPORTED, "packed_linear_noalloc: format %d", a.fmt);
+}
+
+}  // namespace b200
