@@ -14,9 +14,12 @@
  * Conventions (mirroring runtime/support/dx12.py:11-15, which raises on a failed HRESULT):
  *   - every function returns int32 status: 0 = ok, < 0 = error (B200_ERR_*);
  *   - b200_last_error() copies the calling thread's last error message;
- *   - all pointers to tensors are device pointers owned by the caller; the library
- *     allocates nothing on the compute paths (the only allocations are the explicit
- *     b200_malloc / b200_stream_create / b200_event_create calls);
+ *   - all pointers to tensors are device pointers owned by the caller. The compute entry
+ *     points allocate nothing, with one exception: b200_packed_linear on a few tokens
+ *     (3 <= m <= 32) splits K across CTAs and, on its first such call on a (device, stream),
+ *     allocates a 16 MiB split-K workspace kept for the life of the process
+ *     (b200_packed_linear_noalloc is the allocation-free form). Other allocations are the
+ *     explicit b200_malloc / b200_stream_create / b200_event_create calls;
  *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
  *     all compute entry points are asynchronous on that stream.
  *   - thread-safe: no global mutable state on the compute paths except the per-thread
