@@ -136,3 +136,28 @@ def test_public_api_call_forms():
     yc = tg.matmul(w, x.t().contiguous(), dtype=torch.float16)
     assert yc.dtype == torch.float16
     assert_close(yc.t().float().cpu().numpy(), r, "float16")
+
+
+@pytest.mark.parametrize("m", [1, 2])
+def test_e8m0_special_bytes(m):
+    """E8M0 byte 0 (2^-127, an fp32 subnormal) and extreme exponents next to ordinary ones:
+    the decode GEMV converts bytes 1..254 with a shift and must take the exact conversion
+    for byte 0. Row 0 is scaled by 2^-127 everywhere and is compared after rescaling."""
+    from tinygrad_dx12_b200.linalg import _packed_linear
+
+    rng = np.random.default_rng(21)
+    base = ref.make_packed(rng, "fp4_e2m1", 256, 2048, 32, None)
+    e = rng.integers(-10, 11, size=(256, 64))
+    e[0, :] = -127
+    e[1:, ::7] = -127
+    e[5, 3] = -120
+    spec = ref.PackedSpec(base.data, base.format, base.shape, np.exp2(e.astype(np.float64)).astype(np.float32), 32,
+                          "float32")
+    w = to_device(spec, DEV, "e8m0")
+    x = torch.from_numpy(rng.standard_normal((m, 2048)).astype(np.float32)).to(DEV).to(torch.bfloat16)
+    y = _packed_linear(w, x, torch.float32, "gemv").cpu().numpy()
+    wf = ref.dequant(spec.data, spec.format, spec.shape, spec.scales, 32, "float32", "float32")
+    r = x.float().cpu().numpy() @ wf.T
+    assert_close(y[:, 1:], r[:, 1:], "float32")
+    y0, r0 = y[:, 0].astype(np.float64) * 2.0**127, r[:, 0].astype(np.float64) * 2.0**127
+    assert np.all(np.abs(y0 - r0) <= 1e-3 * np.maximum(np.abs(r0), 1.0))

@@ -306,7 +306,30 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (got) {
         read_rows<BITS>(r.lo, base, g, g + 8, sub, t);
         read_rows<BITS>(r.hi, base, g + 16, g + 24, sub, t);
-        if constexpr (GROUP) {
+        if constexpr (SK == SK_E8M0) {
+          // E8M0 bytes 1..254 are 2^(b-127) = float bits b << 23; bytes 0 (2^-127, subnormal)
+          // and 255 (NaN) take the exact conversion (warp-uniform branch, rare)
+          const uint8_t *sb = base + RB * WR;
+          const int blk = sub * 4 + cblk;
+          const uint32_t u0 = *reinterpret_cast<const uint16_t *>(sb + (g * (KSTAGE / 32) + blk));
+          const uint32_t u1 = *reinterpret_cast<const uint16_t *>(sb + ((g + 8) * (KSTAGE / 32) + blk));
+          const uint32_t u2 = *reinterpret_cast<const uint16_t *>(sb + ((g + 16) * (KSTAGE / 32) + blk));
+          const uint32_t u3 = *reinterpret_cast<const uint16_t *>(sb + ((g + 24) * (KSTAGE / 32) + blk));
+          const uint32_t v01 = u0 | (u1 << 16), v23 = u2 | (u3 << 16);
+          const uint32_t special = __vcmpeq4(v01, 0u) | __vcmpeq4(v23, 0u) | __vcmpeq4(v01, 0xFFFFFFFFu) |
+                                   __vcmpeq4(v23, 0xFFFFFFFFu);
+          if (__any_sync(0xffffffffu, special != 0u)) {
+            r.lo.sa0 = e8m0_fast(u0 & 0xFFu), r.lo.sa1 = e8m0_fast(u0 >> 8);
+            r.lo.sb0 = e8m0_fast(u1 & 0xFFu), r.lo.sb1 = e8m0_fast(u1 >> 8);
+            r.hi.sa0 = e8m0_fast(u2 & 0xFFu), r.hi.sa1 = e8m0_fast(u2 >> 8);
+            r.hi.sb0 = e8m0_fast(u3 & 0xFFu), r.hi.sb1 = e8m0_fast(u3 >> 8);
+          } else {
+            r.lo.sa0 = __uint_as_float((u0 & 0xFFu) << 23), r.lo.sa1 = __uint_as_float((u0 & 0xFF00u) << 15);
+            r.lo.sb0 = __uint_as_float((u1 & 0xFFu) << 23), r.lo.sb1 = __uint_as_float((u1 & 0xFF00u) << 15);
+            r.hi.sa0 = __uint_as_float((u2 & 0xFFu) << 23), r.hi.sa1 = __uint_as_float((u2 & 0xFF00u) << 15);
+            r.hi.sb0 = __uint_as_float((u3 & 0xFFu) << 23), r.hi.sb1 = __uint_as_float((u3 & 0xFF00u) << 15);
+          }
+        } else if constexpr (GROUP) {
           const uint8_t *sb = base + RB * WR;
           const int blk = sub * 4 + cblk;  // block index within the stage's 16 blocks per row
           smem_scale_pair<SK>(sb + (g * (KSTAGE / 32) + blk) * SESZ, r.lo.sa0, r.lo.sa1);
