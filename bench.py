@@ -360,7 +360,8 @@ def run_stack(args, device, world, rank):
 
     cfg = S.C5
     layers = cfg.layers if args.stack_layers is None else args.stack_layers
-    st = S.TPStack(cfg, rank, world, device=device, layers=layers, seed=11)
+    ops = S.PeerOps(rows_max=8, hidden=cfg.hidden) if world > 1 else None  # fused peer-memory reduction
+    st = S.TPStack(cfg, rank, world, device=device, layers=layers, seed=11, ops=ops)
     g = torch.Generator(device=device)
     g.manual_seed(5)
     h0 = torch.randn((1, cfg.hidden), device=device, generator=g).to(cfg.act)  # identical on every rank
@@ -395,8 +396,12 @@ def run_stack(args, device, world, rank):
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
     finite = bool(torch.isfinite(h.float()).all().item())
-    del graph  # holds NCCL work: released before the process group
+    del graph  # released before the process group
     torch.cuda.synchronize()
+    if ops is not None:
+        if world > 1:
+            dist.barrier()  # no rank unmaps a buffer a peer may still read
+        ops.close()
     total = cfg.layer_weight_bytes() * layers
     peaks = measured_peaks()
     per_gpu = st.weight_bytes() / (ms / 1e3) / 1e9
@@ -405,8 +410,10 @@ def run_stack(args, device, world, rank):
         "ms_per_token": round(ms, 4), "tokens_per_s": round(1e3 / ms, 2),
         "weight_bytes_per_token": total, "weight_gbs": round(total / (ms / 1e3) / 1e9, 1),
         "per_gpu_weight_gbs": round(per_gpu, 1), "per_gpu_frac_of_hbm": round(per_gpu / peaks["hbm_gbs"], 4),
-        "allreduces_per_token": 2 * layers if world > 1 else 0, "kernels_per_token": layers * 8 + 1,
-        "timing": "CUDA graph of one forward (all layers + NCCL all-reduces), CUDA events, max over ranks",
+        "allreduces_per_token": 2 * layers if world > 1 else 0, "kernels_per_token": layers * 6 + 1,
+        "allreduce": "fused one-shot peer-memory reduction + residual + RMS norm (b200_peer_allreduce_add_rmsnorm)"
+                     if world > 1 else "none",
+        "timing": "CUDA graph of one forward (all layers), CUDA events, max over ranks",
         "output_finite": finite,
     }
 

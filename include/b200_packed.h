@@ -204,6 +204,25 @@ int32_t b200_add_rmsnorm(void *h, int32_t h_dtype, const float *partial, void *x
 int32_t b200_gate_mul(const void *gu, int32_t gu_dtype, void *out, int32_t out_dtype, int64_t M, int64_t I,
                       void *stream);
 
+/* Tensor-parallel reduction of the row-parallel projections over peer memory, fused with the
+ * residual add and RMS norm (the all-reduce step of the stacks). No counterpart in the
+ * reference. `partials[q]` is rank q's fp32 partial (M x H rows, row-major) as mapped in this
+ * process, `flags[q]` rank q's flag array (world x rows_max uint32, zeroed before first use),
+ * `epoch` this rank's counters (rows_max uint32, zeroed before first use). Per row the kernel
+ * publishes its epoch to every rank, waits for every rank's (giving up after timeout_ns with
+ * the device error bit set), then h += sum over q = 0..world-1 of partials[q] (fixed order)
+ * and x = h * rsqrt(mean(h^2) + eps). M <= rows_max, world <= 8. */
+int32_t b200_peer_allreduce_add_rmsnorm(const void *const *partials, uint32_t *const *flags, uint32_t *epoch,
+                                        int32_t rank, int32_t world, int64_t rows_max, int64_t timeout_ns, void *h,
+                                        int32_t h_dtype, void *x, int32_t x_dtype, int64_t M, int64_t H, float eps,
+                                        void *stream);
+
+/* CUDA IPC plumbing for the peer buffers: export a handle (64 bytes) of a b200_malloc'd
+ * allocation, open a peer's handle in this process, close it. */
+int32_t b200_ipc_get_handle(void *dev_ptr, void *handle64);
+int32_t b200_ipc_open(const void *handle64, void **dev_ptr);
+int32_t b200_ipc_close(void *dev_ptr);
+
 #ifdef __cplusplus
 }
 #endif

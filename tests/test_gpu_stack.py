@@ -64,3 +64,39 @@ def _cuda(w):
     from tinygrad_dx12_b200.packed import PackedTensor
 
     return PackedTensor(w.data.to(DEV), w.format, w.shape, None if w.scales is None else w.scales.to(DEV), w.block_size)
+
+
+def test_peer_reduce_single_rank_matches_add_rmsnorm():
+    """b200_peer_allreduce_add_rmsnorm with one rank (it waits only on its own flag) equals
+    b200_add_rmsnorm of the same partial over several epochs and both buffers."""
+    import ctypes
+
+    from tinygrad_dx12_b200 import _lib
+    from tinygrad_dx12_b200 import dtypes as D
+    from tinygrad_dx12_b200.packed import stream_ptr
+
+    rows_max, hidden = 4, 4096
+    part = torch.zeros((2, rows_max, hidden), dtype=torch.float32, device=DEV)
+    flags = torch.zeros(rows_max, dtype=torch.int32, device=DEV)
+    epoch = torch.zeros(rows_max, dtype=torch.int32, device=DEV)
+    P = ctypes.c_void_p * 8
+    g = torch.Generator(device=DEV).manual_seed(3)
+    h = torch.randn((3, hidden), device=DEV, generator=g).to(torch.bfloat16)
+    h_ref = h.clone()
+    x = torch.empty_like(h)
+    x_ref = torch.empty_like(h)
+    for step in range(5):
+        slot = step % 2
+        part[slot, :3] = torch.randn((3, hidden), device=DEV, generator=g)
+        _lib.call("b200_peer_allreduce_add_rmsnorm", P(part[slot].data_ptr()), P(flags.data_ptr()), epoch.data_ptr(),
+                  0, 1, rows_max, int(1e9), h.data_ptr(), _lib.DT[D.name(h.dtype)], x.data_ptr(),
+                  _lib.DT[D.name(x.dtype)], 3, hidden, S.EPS, stream_ptr(h.device))
+        S.CudaOps().add_rmsnorm(h_ref, part[slot, :3].contiguous(), x_ref)
+        torch.cuda.synchronize()
+        assert torch.equal(h, h_ref)  # the residual sum is elementwise: bitwise equal
+        # x: the sum of squares is reduced in a different thread order -> within 2 bf16 ulps
+        assert (x.float() - x_ref.float()).abs().max().item() <= 2 * 2**-7 * x_ref.float().abs().max().item()
+    assert epoch[:3].tolist() == [5, 5, 5] and flags[:3].tolist() == [5, 5, 5]
+    v = ctypes.c_uint32(0)
+    _lib.call("b200_device_status", 0, ctypes.byref(v), 1)
+    assert v.value == 0

@@ -69,6 +69,11 @@ SIGNATURES = {
     "b200_event_destroy": ([_P], _I32),
     "b200_device_wait_flag": ([_P, _I32, _I64, _P, _P], _I32),
     "b200_packed_linear_noalloc": ([_DESC, _P, _I32, _I64, _I64, _P, _I32, _I64, _P], _I32),
+    "b200_peer_allreduce_add_rmsnorm": ([_P, _P, _P, _I32, _I32, _I64, _I64, _P, _I32, _P, _I32, _I64, _I64,
+                                         ctypes.c_float, _P], _I32),
+    "b200_ipc_get_handle": ([_P, _P], _I32),
+    "b200_ipc_open": ([_P, ctypes.POINTER(_P)], _I32),
+    "b200_ipc_close": ([_P], _I32),
     "b200_add_rmsnorm": ([_P, _I32, _P, _P, _I32, _I64, _I64, ctypes.c_float, _P], _I32),
     "b200_gate_mul": ([_P, _I32, _P, _I32, _I64, _I64, _P], _I32),
     "b200_device_status": ([_I32, ctypes.POINTER(ctypes.c_uint32), _I32], _I32),

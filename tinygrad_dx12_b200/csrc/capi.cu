@@ -288,9 +288,10 @@ int32_t b200_device_status(int32_t device, uint32_t *flags, int32_t clear) {
   unsigned int v = 0, u = 0;
   if (int32_t rc = gemm_device_error(&v, clear != 0)) return rc;
   if (int32_t rc = gemv_device_error(&u, clear != 0)) return rc;
-  unsigned int w = 0;
+  unsigned int w = 0, z = 0;
   if (int32_t rc = skinny_device_error(&w, clear != 0)) return rc;
-  *flags = v | u | w;
+  if (int32_t rc = stackops_device_error(&z, clear != 0)) return rc;
+  *flags = v | u | w | z;
   return B200_OK;
 }
 
@@ -327,6 +328,45 @@ int32_t b200_gate_mul(const void *gu, int32_t gu_dtype, void *out, int32_t out_d
   if (!dt_is_float(gu_dtype) || !dt_is_float(out_dtype))
     return b200_set_error(B200_ERR_INVALID, "gate_mul needs floating-point tensors");
   return launch_gate_mul(gu, gu_dtype, out, out_dtype, M, I, (cudaStream_t)stream);
+}
+
+int32_t b200_peer_allreduce_add_rmsnorm(const void *const *partials, uint32_t *const *flags, uint32_t *epoch,
+                                        int32_t rank, int32_t world, int64_t rows_max, int64_t timeout_ns, void *h,
+                                        int32_t h_dtype, void *x, int32_t x_dtype, int64_t M, int64_t H, float eps,
+                                        void *stream) {
+  if (int32_t rc = injected()) return rc;
+  if (partials == nullptr || flags == nullptr || epoch == nullptr || h == nullptr)
+    return b200_set_error(B200_ERR_INVALID, "peer reduce: null pointer");
+  if (world < 1 || world > 8 || rank < 0 || rank >= world || M < 0 || M > rows_max || H < 0 || timeout_ns <= 0)
+    return b200_set_error(B200_ERR_INVALID, "peer reduce: bad rank/world/rows/timeout");
+  for (int q = 0; q < world; ++q)
+    if (partials[q] == nullptr || flags[q] == nullptr) return b200_set_error(B200_ERR_INVALID, "peer reduce: null peer");
+  if (!dt_is_float(h_dtype) || (x != nullptr && !dt_is_float(x_dtype)))
+    return b200_set_error(B200_ERR_INVALID, "peer reduce needs floating-point h / x");
+  return launch_peer_reduce_rmsnorm(partials, flags, epoch, rank, world, rows_max, timeout_ns, h, h_dtype, x, x_dtype, M,
+                                    H, eps, (cudaStream_t)stream);
+}
+
+int32_t b200_ipc_get_handle(void *dev_ptr, void *handle64) {
+  if (dev_ptr == nullptr || handle64 == nullptr) return b200_set_error(B200_ERR_INVALID, "ipc: null pointer");
+  cudaIpcMemHandle_t hd;
+  B200_CUDA_TRY(cudaIpcGetMemHandle(&hd, dev_ptr));
+  memcpy(handle64, &hd, sizeof(hd));
+  return B200_OK;
+}
+
+int32_t b200_ipc_open(const void *handle64, void **dev_ptr) {
+  if (dev_ptr == nullptr || handle64 == nullptr) return b200_set_error(B200_ERR_INVALID, "ipc: null pointer");
+  cudaIpcMemHandle_t hd;
+  memcpy(&hd, handle64, sizeof(hd));
+  B200_CUDA_TRY(cudaIpcOpenMemHandle(dev_ptr, hd, cudaIpcMemLazyEnablePeerAccess));
+  return B200_OK;
+}
+
+int32_t b200_ipc_close(void *dev_ptr) {
+  if (dev_ptr == nullptr) return b200_set_error(B200_ERR_INVALID, "ipc: null pointer");
+  B200_CUDA_TRY(cudaIpcCloseMemHandle(dev_ptr));
+  return B200_OK;
 }
 
 int32_t b200_device_wait_flag(const int32_t *flag, int32_t expect, int64_t max_spins, int32_t *status, void *stream) {

@@ -62,6 +62,10 @@ int32_t launch_matmul_generic(const void *a, int adt, int64_t sam, int64_t sak, 
 int32_t launch_cast(const void *src, int sdt, void *dst, int ddt, int64_t n, cudaStream_t stream);
 int32_t launch_add_rmsnorm(void *h, int hdt, const float *partial, void *x, int xdt, int64_t M, int64_t H, float eps,
                            cudaStream_t stream);
+int32_t launch_peer_reduce_rmsnorm(const void *const *partials, uint32_t *const *flags, uint32_t *epoch, int rank,
+                                   int world, int64_t rows_max, int64_t timeout_ns, void *h, int hdt, void *x, int xdt,
+                                   int64_t M, int64_t H, float eps, cudaStream_t stream);
+int32_t stackops_device_error(unsigned int *v, bool clear);
 int32_t launch_gate_mul(const void *gu, int gdt, void *out, int odt, int64_t M, int64_t I, cudaStream_t stream);
 int32_t launch_wait_flag(const int32_t *flag, int32_t expect, int64_t max_spins, int32_t *status, cudaStream_t stream);
 

@@ -6,6 +6,7 @@
 // so the multi-layer configurations run without a torch elementwise chain between kernels.
 #include "common.cuh"
 #include "kernels.h"
+#include "sm100.cuh"
 
 namespace b200 {
 namespace stackops {
@@ -78,6 +79,179 @@ int32_t launch_gate_mul(const void *gu, int gdt, void *out, int odt, int64_t M, 
   int64_t blocks = (n + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   stackops::gate_mul_kernel<<<(unsigned)blocks, 256, 0, stream>>>(gu, gdt, out, odt, M, I);
+  B200_LAUNCH_CHECK();
+  return B200_OK;
+}
+
+}  // namespace b200
+
+// ---- tensor-parallel reduction over peer memory (one-shot, fused with add + RMS norm) -------
+// Each rank's row-parallel projection has written its fp32 partial (M x H) into its own buffer,
+// which every peer has mapped (CUDA IPC). For row r, CTA r:
+//   1. e = ++epoch[r] (this rank's count of reductions of row r; the same on every rank);
+//   2. publishes e in flags[rank][r] of every rank (release, system scope);
+//   3. waits until flags[q][r] >= e locally for every rank q (bounded; on give-up it flags the
+//      device error word and continues);
+//   4. sums the partial rows of ranks 0..world-1 in that order (identical on every rank, so h
+//      stays bitwise replicated), adds the sum to h and writes x = rmsnorm(h).
+// A rank reuses a partial buffer only two reductions later, after every peer has signalled
+// the reduction in between, i.e. after every peer has finished reading it.
+
+namespace b200 {
+
+int32_t stackops_device_error(unsigned int *v, bool clear) {
+  B200_CUDA_TRY(tu_device_error(v, clear));
+  return B200_OK;
+}
+
+namespace stackops {
+
+constexpr int MAX_PEERS = 8;
+struct PeerReduce {
+  const float *partial[MAX_PEERS];  // rank q's partial buffer (M x H fp32), mapped here
+  uint32_t *flags[MAX_PEERS];       // rank q's flag array [world][rows_max], mapped here
+  uint32_t *epoch;                  // this rank's epoch counters [rows_max]
+  int rank, world;
+  int64_t rows_max;
+  int64_t timeout_ns;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+constexpr int PR_THREADS = 1024;
+constexpr int PR_VEC = 2;  // float4 per thread per rank held in registers at once (H <= 8192 per pass)
+
+template <typename T>
+__device__ __forceinline__ float round_to(float v);
+template <>
+__device__ __forceinline__ float round_to<__half>(float v) { return __half2float(__float2half_rn(v)); }
+template <>
+__device__ __forceinline__ float round_to<__nv_bfloat16>(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+template <>
+__device__ __forceinline__ float round_to<float>(float v) { return v; }
+
+template <typename T>
+__global__ void __launch_bounds__(PR_THREADS) peer_reduce_rmsnorm_kernel(PeerReduce pr, T *__restrict__ h,
+                                                                         void *x, int xdt, int64_t H, float eps) {
+  __shared__ float red[PR_THREADS / 32 + 1];
+  const int64_t row = blockIdx.x;
+  if (threadIdx.x == 0) {
+    const uint32_t e = pr.epoch[row] + 1u;
+    pr.epoch[row] = e;
+    __threadfence_system();  // this rank's partial (written by the previous kernel) before the flags
+    for (int q = 0; q < pr.world; ++q) st_release_sys(pr.flags[q] + (int64_t)pr.rank * pr.rows_max + row, e);
+    const uint32_t *mine = pr.flags[pr.rank];
+    const uint64_t t0 = globaltimer();
+    for (int q = 0; q < pr.world; ++q) {
+      for (uint32_t i = 0;; ++i) {
+        if ((int32_t)(ld_acquire_sys(mine + (int64_t)q * pr.rows_max + row) - e) >= 0) break;
+        if ((i & 255u) == 255u && globaltimer() - t0 > (uint64_t)pr.timeout_ns) {
+          atomicOr(&g_device_error, B200_DEVERR_MBAR_TIMEOUT);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  T *hr = h + row * H;
+  const int64_t base = row * H;
+  float ss = 0.f;
+  if (H % 4 == 0) {
+    const int64_t nv = H / 4;
+    for (int64_t v0 = 0; v0 < nv; v0 += (int64_t)PR_THREADS * PR_VEC) {
+      float4 acc[PR_VEC];
+      float4 got[MAX_PEERS][PR_VEC];
+#pragma unroll
+      for (int q = 0; q < MAX_PEERS; ++q)  // every peer load issued before any is used
+#pragma unroll
+        for (int u = 0; u < PR_VEC; ++u) {
+          const int64_t v = v0 + threadIdx.x + (int64_t)u * PR_THREADS;
+          got[q][u] = (q < pr.world && v < nv) ? __ldcv(reinterpret_cast<const float4 *>(pr.partial[q] + base) + v)
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+      for (int u = 0; u < PR_VEC; ++u) {
+        acc[u] = got[0][u];
+#pragma unroll
+        for (int q = 1; q < MAX_PEERS; ++q)
+          if (q < pr.world) acc[u].x += got[q][u].x, acc[u].y += got[q][u].y, acc[u].z += got[q][u].z, acc[u].w += got[q][u].w;
+        const int64_t v = v0 + threadIdx.x + (int64_t)u * PR_THREADS;
+        if (v < nv) {
+          const float r[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const float hv = round_to<T>((float)hr[4 * v + c] + r[c]);
+            hr[4 * v + c] = (T)hv;
+            ss += hv * hv;
+          }
+        }
+      }
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < H; i += PR_THREADS) {
+      float sum = 0.f;
+      for (int q = 0; q < pr.world; ++q) sum += __ldcv(pr.partial[q] + base + i);
+      const float hv = round_to<T>((float)hr[i] + sum);
+      hr[i] = (T)hv;
+      ss += hv * hv;
+    }
+  }
+  // block sum of squares
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < PR_THREADS / 32 ? red[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lane == 0) red[PR_THREADS / 32] = t;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[PR_THREADS / 32] / (float)H + eps);
+  if (x != nullptr)
+    for (int64_t i = threadIdx.x; i < H; i += PR_THREADS) store_f32(x, base + i, xdt, (float)hr[i] * inv);
+}
+
+}  // namespace stackops
+
+int32_t launch_peer_reduce_rmsnorm(const void *const *partials, uint32_t *const *flags, uint32_t *epoch, int rank,
+                                   int world, int64_t rows_max, int64_t timeout_ns, void *h, int hdt, void *x, int xdt,
+                                   int64_t M, int64_t H, float eps, cudaStream_t stream) {
+  if (M <= 0 || H <= 0) return B200_OK;
+  stackops::PeerReduce pr = {};
+  for (int q = 0; q < world; ++q) {
+    pr.partial[q] = static_cast<const float *>(partials[q]);
+    pr.flags[q] = flags[q];
+  }
+  pr.epoch = epoch;
+  pr.rank = rank;
+  pr.world = world;
+  pr.rows_max = rows_max;
+  pr.timeout_ns = timeout_ns;
+  using namespace stackops;
+  switch (hdt) {
+    case B200_DT_F16:
+      peer_reduce_rmsnorm_kernel<__half><<<(unsigned)M, PR_THREADS, 0, stream>>>(pr, (__half *)h, x, xdt, H, eps);
+      break;
+    case B200_DT_BF16:
+      peer_reduce_rmsnorm_kernel<__nv_bfloat16>
+          <<<(unsigned)M, PR_THREADS, 0, stream>>>(pr, (__nv_bfloat16 *)h, x, xdt, H, eps);
+      break;
+    case B200_DT_F32:
+      peer_reduce_rmsnorm_kernel<float><<<(unsigned)M, PR_THREADS, 0, stream>>>(pr, (float *)h, x, xdt, H, eps);
+      break;
+    default:
+      return b200_set_error(B200_ERR_UNSUPPORTED, "peer reduce: h dtype %d (f16, bf16, f32)", hdt);
+  }
   B200_LAUNCH_CHECK();
   return B200_OK;
 }

@@ -185,6 +185,100 @@ class CudaOps:
         if dist.is_initialized() and dist.get_world_size(self.group) > 1:
             dist.all_reduce(t, group=self.group)
 
+    def row_reduce(self, w: PackedTensor, inp: torch.Tensor, h: torch.Tensor, x: torch.Tensor, slot: int) -> None:
+        """h += allreduce(inp @ w^T) (fp32 partials); x = rmsnorm(h)."""
+        p = self.linear(w, inp, torch.float32)
+        self.all_reduce(p)
+        self.add_rmsnorm(h, p, x)
+
+
+class PeerReducer:
+    """Partial buffers shared by all ranks through CUDA IPC, and the fused one-shot reduction.
+
+    Per rank one device allocation holds two fp32 partial buffers (rows_max x hidden), the
+    flag words every rank writes into ([world][rows_max]) and this rank's epoch counters. The
+    allocation's IPC handle is exchanged over the process group; each rank maps every peer's.
+    """
+
+    def __init__(self, rows_max: int, hidden: int, group=None, timeout_s: float = 5.0):
+        import ctypes
+
+        import torch.distributed as dist
+
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("peer reduction supports up to 8 ranks")
+        self.rows_max, self.hidden, self.group = rows_max, hidden, group
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.dev = torch.cuda.current_device()
+        self.part_bytes = rows_max * hidden * 4
+        flag_bytes = self.world * rows_max * 4
+        total = 2 * self.part_bytes + flag_bytes + rows_max * 4
+        base = ctypes.c_void_p()
+        _lib.call("b200_malloc", self.dev, total, ctypes.byref(base))
+        self.base = base.value
+        zeros = torch.zeros(total, dtype=torch.uint8, device=f"cuda:{self.dev}")
+        _lib.call("b200_memcpy", self.base, zeros.data_ptr(), total, 2, None)
+        torch.cuda.synchronize()
+        handle = ctypes.create_string_buffer(64)
+        _lib.call("b200_ipc_get_handle", self.base, handle)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self.bases, self.opened = [], []
+        for q, hq in enumerate(handles):
+            if q == self.rank:
+                self.bases.append(self.base)
+                continue
+            p = ctypes.c_void_p()
+            _lib.call("b200_ipc_open", ctypes.create_string_buffer(hq, 64), ctypes.byref(p))
+            self.bases.append(p.value)
+            self.opened.append(p.value)
+        P = ctypes.c_void_p * 8
+        self._partials = [P(*[b + slot * self.part_bytes for b in self.bases]) for slot in (0, 1)]
+        self._flags = P(*[b + 2 * self.part_bytes for b in self.bases])
+        self.epoch = self.base + 2 * self.part_bytes + flag_bytes
+        dist.barrier(group=group)  # every rank's flags are zero before anyone signals
+
+    def partial_ptr(self, slot: int) -> int:
+        return self.base + slot * self.part_bytes
+
+    def reduce(self, slot: int, h: torch.Tensor, x: torch.Tensor | None) -> None:
+        m, hidden = h.shape
+        if m > self.rows_max or hidden != self.hidden:
+            raise ValueError("peer reduction: rows or width beyond the shared buffers")
+        _lib.call("b200_peer_allreduce_add_rmsnorm", self._partials[slot], self._flags, self.epoch, self.rank,
+                  self.world, self.rows_max, self.timeout_ns, h.data_ptr(), _lib.DT[D.name(h.dtype)],
+                  x.data_ptr() if x is not None else None, _lib.DT[D.name(x.dtype)] if x is not None else 0, m, hidden,
+                  EPS, stream_ptr(h.device))
+
+    def close(self) -> None:
+        for p in self.opened:
+            _lib.call("b200_ipc_close", p)
+        self.opened = []
+        if self.base:
+            _lib.call("b200_free", self.dev, self.base)
+            self.base = 0
+
+
+class PeerOps(CudaOps):
+    """CudaOps whose row-parallel projections write fp32 partials straight into the shared
+    buffers and reduce them with the fused peer-memory kernel (rows <= rows_max)."""
+
+    def __init__(self, rows_max: int, hidden: int, group=None):
+        super().__init__(group)
+        self.reducer = PeerReducer(rows_max, hidden, group)
+
+    def row_reduce(self, w: PackedTensor, inp: torch.Tensor, h: torch.Tensor, x: torch.Tensor, slot: int) -> None:
+        from .linalg import _packed_linear_into
+
+        if h.shape[0] > self.reducer.rows_max:  # beyond the shared buffers: NCCL all-reduce
+            return super().row_reduce(w, inp, h, x, slot)
+        _packed_linear_into(w, inp, self.reducer.partial_ptr(slot), torch.float32, h.shape[1])
+        self.reducer.reduce(slot, h, x)
+
+    def close(self) -> None:
+        self.reducer.close()
+
 
 class TPStack:
     """One rank's shard of a packed projection stack and its forward pass."""
@@ -216,15 +310,18 @@ class TPStack:
         x = torch.empty_like(h)
         mbuf = torch.empty((m, self.layers[0].inter_rows if self.layers else 0), dtype=cfg.act, device=h.device)
         ops.add_rmsnorm(h, None, x)
+        row_reduce = getattr(ops, "row_reduce", None) or (lambda w, inp, hh, xx, slot: _generic_row_reduce(ops, w, inp,
+                                                                                                           hh, xx))
         for L in self.layers:
             qkv = ops.linear(L.qkv, x, cfg.act)
-            q = qkv[:, :L.q_rows]
-            po = ops.linear(L.o, q, torch.float32)
-            ops.all_reduce(po)
-            ops.add_rmsnorm(h, po, x)
+            row_reduce(L.o, qkv[:, :L.q_rows], h, x, 0)
             gu = ops.linear(L.gu, x, cfg.act)
             ops.gate_mul(gu, mbuf)
-            pd = ops.linear(L.down, mbuf, torch.float32)
-            ops.all_reduce(pd)
-            ops.add_rmsnorm(h, pd, x)
+            row_reduce(L.down, mbuf, h, x, 1)
         return h
+
+
+def _generic_row_reduce(ops, w, inp, h, x) -> None:
+    p = ops.linear(w, inp, torch.float32)
+    ops.all_reduce(p)
+    ops.add_rmsnorm(h, p, x)
