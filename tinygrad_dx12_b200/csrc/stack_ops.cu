@@ -32,9 +32,33 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 
 // One CTA per row: h = h + partial (if given, fp32 add then rounding to h's dtype);
 // x = h * rsqrt(mean(h^2) + eps) in fp32, stored in x's dtype.
+__device__ __forceinline__ void pdl_enter() {
+  // launched with programmatic stream serialization: let the next kernel start its prologue,
+  // then wait until the previous kernel's results are visible before reading them
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Launch with the programmatic-dependent-launch attribute (every kernel here calls pdl_enter
+// before touching memory, so the attribute is always safe).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 __global__ void __launch_bounds__(THREADS) add_rmsnorm_kernel(void *h, int hdt, const float *partial, void *x,
                                                               int xdt, int64_t H, float eps) {
   __shared__ float red[THREADS / 32 + 1];
+  pdl_enter();
   const int64_t row = blockIdx.x;
   const int64_t base = row * H;
   float ss = 0.f;
@@ -55,6 +79,7 @@ __global__ void __launch_bounds__(THREADS) add_rmsnorm_kernel(void *h, int hdt, 
 
 // out[m, i] = gu[m, i] * gu[m, I + i] (fp32 product, rounded to out's dtype).
 __global__ void gate_mul_kernel(const void *gu, int gdt, void *out, int odt, int64_t M, int64_t I) {
+  pdl_enter();
   const int64_t n = M * I;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t m = t / I, i = t - m * I;
@@ -68,8 +93,8 @@ __global__ void gate_mul_kernel(const void *gu, int gdt, void *out, int odt, int
 int32_t launch_add_rmsnorm(void *h, int hdt, const float *partial, void *x, int xdt, int64_t M, int64_t H, float eps,
                            cudaStream_t stream) {
   if (M <= 0 || H <= 0) return B200_OK;
-  stackops::add_rmsnorm_kernel<<<(unsigned)M, stackops::THREADS, 0, stream>>>(h, hdt, partial, x, xdt, H, eps);
-  B200_LAUNCH_CHECK();
+  B200_CUDA_TRY(stackops::launch_pdl(stackops::add_rmsnorm_kernel, dim3((unsigned)M), dim3(stackops::THREADS), stream, h,
+                                     hdt, partial, x, xdt, H, eps));
   return B200_OK;
 }
 
@@ -78,8 +103,8 @@ int32_t launch_gate_mul(const void *gu, int gdt, void *out, int odt, int64_t M, 
   if (n <= 0) return B200_OK;
   int64_t blocks = (n + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  stackops::gate_mul_kernel<<<(unsigned)blocks, 256, 0, stream>>>(gu, gdt, out, odt, M, I);
-  B200_LAUNCH_CHECK();
+  B200_CUDA_TRY(stackops::launch_pdl(stackops::gate_mul_kernel, dim3((unsigned)blocks), dim3(256), stream, gu, gdt, out,
+                                     odt, M, I));
   return B200_OK;
 }
 
@@ -142,6 +167,7 @@ __global__ void __launch_bounds__(PR_THREADS) peer_reduce_rmsnorm_kernel(PeerRed
                                                                          void *x, int xdt, int64_t H, float eps) {
   __shared__ float red[PR_THREADS / 32 + 1];
   const int64_t row = blockIdx.x;
+  pdl_enter();  // this rank's partial is complete from here on
   if (threadIdx.x == 0) {
     const uint32_t e = pr.epoch[row] + 1u;
     pr.epoch[row] = e;
@@ -240,19 +266,20 @@ int32_t launch_peer_reduce_rmsnorm(const void *const *partials, uint32_t *const 
   using namespace stackops;
   switch (hdt) {
     case B200_DT_F16:
-      peer_reduce_rmsnorm_kernel<__half><<<(unsigned)M, PR_THREADS, 0, stream>>>(pr, (__half *)h, x, xdt, H, eps);
+      B200_CUDA_TRY(launch_pdl(peer_reduce_rmsnorm_kernel<__half>, dim3((unsigned)M), dim3(PR_THREADS), stream, pr,
+                               (__half *)h, x, xdt, H, eps));
       break;
     case B200_DT_BF16:
-      peer_reduce_rmsnorm_kernel<__nv_bfloat16>
-          <<<(unsigned)M, PR_THREADS, 0, stream>>>(pr, (__nv_bfloat16 *)h, x, xdt, H, eps);
+      B200_CUDA_TRY(launch_pdl(peer_reduce_rmsnorm_kernel<__nv_bfloat16>, dim3((unsigned)M), dim3(PR_THREADS), stream,
+                               pr, (__nv_bfloat16 *)h, x, xdt, H, eps));
       break;
     case B200_DT_F32:
-      peer_reduce_rmsnorm_kernel<float><<<(unsigned)M, PR_THREADS, 0, stream>>>(pr, (float *)h, x, xdt, H, eps);
+      B200_CUDA_TRY(launch_pdl(peer_reduce_rmsnorm_kernel<float>, dim3((unsigned)M), dim3(PR_THREADS), stream, pr,
+                               (float *)h, x, xdt, H, eps));
       break;
     default:
       return b200_set_error(B200_ERR_UNSUPPORTED, "peer reduce: h dtype %d (f16, bf16, f32)", hdt);
   }
-  B200_LAUNCH_CHECK();
   return B200_OK;
 }
 

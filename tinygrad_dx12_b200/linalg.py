@@ -90,27 +90,27 @@ def _aligned_x(x: torch.Tensor) -> torch.Tensor:
     return buf[:, :k]
 
 
-def _packed_linear(w: PackedTensor, x: torch.Tensor, out_dtype: torch.dtype, path: str) -> torch.Tensor:
-    """y[M, N] = x[M, K] @ dequant(W)[N, K]^T through ``b200_packed_linear``."""
+def _packed_linear(w: PackedTensor, x: torch.Tensor, out_dtype: torch.dtype, path: str, flags: int = 0) -> torch.Tensor:
+    """y[M, N] = x[M, K] @ dequant(W)[N, K]^T through ``b200_packed_linear`` (``flags``: B200_FLAG_*)."""
     x = _aligned_x(x)
     m = x.shape[0]
     ldx = x.stride(0) if m > 1 else -(-x.shape[1] // 8) * 8
     y = torch.empty((m, w.rows), device=x.device, dtype=out_dtype)
     d = w.desc()
     _lib.call("b200_packed_linear", ctypes_ref(d), x.data_ptr(), _lib.DT[D.name(x.dtype)], m, ldx, 1,
-              y.data_ptr(), _lib.DT[D.name(out_dtype)], y.stride(0), 1, _lib.PATH[path], stream_ptr(x.device))
+              y.data_ptr(), _lib.DT[D.name(out_dtype)], y.stride(0), 1, _lib.PATH[path] | flags, stream_ptr(x.device))
     return y
 
 
 def _packed_linear_into(w: PackedTensor, x: torch.Tensor, y_ptr: int, out_dtype: torch.dtype, ldy: int,
-                        path: str = "auto") -> None:
+                        path: str = "auto", flags: int = 0) -> None:
     """Like ``_packed_linear`` but into caller-owned device memory (row-major, row pitch ``ldy``)."""
     x = _aligned_x(x)
     m = x.shape[0]
     ldx = x.stride(0) if m > 1 else -(-x.shape[1] // 8) * 8
     d = w.desc()
     _lib.call("b200_packed_linear", ctypes_ref(d), x.data_ptr(), _lib.DT[D.name(x.dtype)], m, ldx, 1, y_ptr,
-              _lib.DT[D.name(out_dtype)], ldy, 1, _lib.PATH[path], stream_ptr(x.device))
+              _lib.DT[D.name(out_dtype)], ldy, 1, _lib.PATH[path] | flags, stream_ptr(x.device))
 
 
 def linear_plan(w: PackedTensor, x_dtype: torch.dtype, m: int, out_dtype: torch.dtype, path: str = "auto") -> str | None:

@@ -34,6 +34,7 @@ from . import dtypes as D
 from .packed import FORMATS, PackedTensor, stream_ptr
 
 EPS = 1e-6
+FLAG_PDL = 0x100  # B200_FLAG_PDL: the decode GEMV may start streaming weights while the previous kernel ends
 
 
 @dataclasses.dataclass(frozen=True)
@@ -166,7 +167,7 @@ class CudaOps:
     def linear(self, w: PackedTensor, x: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
         from .linalg import _packed_linear
 
-        return _packed_linear(w, x, out_dtype, "auto")
+        return _packed_linear(w, x, out_dtype, "auto", FLAG_PDL if x.shape[0] <= 2 else 0)
 
     def add_rmsnorm(self, h: torch.Tensor, partial: torch.Tensor | None, x_out: torch.Tensor | None) -> None:
         _lib.call("b200_add_rmsnorm", h.data_ptr(), _lib.DT[D.name(h.dtype)],
@@ -273,7 +274,8 @@ class PeerOps(CudaOps):
 
         if h.shape[0] > self.reducer.rows_max:  # beyond the shared buffers: NCCL all-reduce
             return super().row_reduce(w, inp, h, x, slot)
-        _packed_linear_into(w, inp, self.reducer.partial_ptr(slot), torch.float32, h.shape[1])
+        _packed_linear_into(w, inp, self.reducer.partial_ptr(slot), torch.float32, h.shape[1], "auto",
+                            FLAG_PDL if inp.shape[0] <= 2 else 0)
         self.reducer.reduce(slot, h, x)
 
     def close(self) -> None:
