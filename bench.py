@@ -144,7 +144,10 @@ def make_weights(cfg, device, copies: int, seed: int):
             e = torch.randint(-8, -1, (n, k // cfg["block"]), device=device, generator=g)
             scales = (e + 127).to(torch.uint8).view(torch.float8_e8m0fnu)
             ws.append(tg.PackedTensor(data, cfg["fmt"], (n, k), scales, cfg["block"]))
-        else:
+        elif cfg["scale"] == "f16u":  # per-block fp16 ~U(0.005, 0.02)
+            s = torch.rand((n, k // cfg["block"]), device=device, generator=g) * 0.015 + 0.005
+            ws.append(tg.PackedTensor(data, cfg["fmt"], (n, k), s.to(torch.float16), cfg["block"]))
+        else:  # per-row fp16 ~U(0.01, 0.05)
             s = torch.rand((n, 1), device=device, generator=g) * 0.04 + 0.01
             ws.append(tg.PackedTensor(data, cfg["fmt"], (n, k), s.to(torch.float16), k))
     return ws
@@ -245,6 +248,9 @@ def run_gpu_arm(args, world, rank, local):
     stack = None
     if not args.no_stack:
         stack = run_stack(args, device, world, rank)
+    configs = None
+    if not args.no_configs:
+        configs = run_configs(args, device, world, rank)
     peaks = measured_peaks()
     result = None
     if rank == 0:
@@ -284,10 +290,135 @@ def run_gpu_arm(args, world, rank, local):
             result["gemm"] = gemm
         if stack is not None:
             result["stack"] = stack
+        if configs is not None:
+            result["configs"] = configs
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return result
+
+
+def _graph_time_ms(launch, steps: int, device) -> float:
+    """Average ms per launch of a CUDA graph of `steps` launches (warm-up launches first)."""
+    import torch
+
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            launch(i, stream.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(steps):
+            launch(i, stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    del graph
+    return e0.elapsed_time(e1) / steps
+
+
+def run_configs(args, device, world, rank):
+    """The other headline configurations, one GPU each (every rank measures its own; rank 0's
+    line reports the max time over ranks): c1 INT4 M=1, c2 FP4 M=8 / 32, one c5 layer's
+    projections at M=2048 and the c4 INT4 stack at M=1 (one token through 32 layers)."""
+    import torch
+    import torch.distributed as dist
+    from tinygrad_dx12_b200 import _lib
+    from tinygrad_dx12_b200 import stack as S
+    from tinygrad_dx12_b200.linalg import linear_plan
+
+    peaks = measured_peaks()
+    fn = _lib.lib().b200_packed_linear
+    out = {}
+
+    def max_ms(ms):
+        t = torch.tensor([ms], device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def gemv_case(name, cfg, copies, steps):
+        ws = make_weights(cfg, device, copies, seed=7 + rank)
+        xdt = getattr(torch, cfg["xdt"])
+        x = torch.randn((cfg["m"], cfg["k"]), device=device).to(xdt)
+        y = torch.empty((cfg["m"], cfg["n"]), device=device, dtype=xdt)
+        descs = [w.desc() for w in ws]
+        code = _lib.DT[cfg["xdt"]]
+        flags = 0x100 if cfg["m"] <= 2 else 0
+
+        def launch(i, stream):
+            rc = fn(ctypes.byref(descs[i % copies]), x.data_ptr(), code, cfg["m"], cfg["k"], 1, y.data_ptr(), code,
+                    cfg["n"], 1, flags, stream)
+            if rc:
+                raise RuntimeError(_lib.last_error())
+
+        ms = max_ms(_graph_time_ms(launch, steps, device))
+        gbs = algo_bytes(cfg) / (ms / 1e3) / 1e9
+        out[name] = {"us_per_call": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                     "kernel": linear_plan(ws[0], xdt, cfg["m"], xdt), "algorithmic_bytes": algo_bytes(cfg),
+                     "l2": f"{copies} rotating weight copies (> 4 x L2)"}
+        del ws
+
+    c1 = dict(fmt="int4", n=4096, k=4096, block=32, scale="f16u", xdt="float16", m=1)
+    gemv_case("c1_int4_m1", c1, copies=64, steps=max(20, min(args.steps, 200)))
+    for m in (8, 32):
+        gemv_case(f"c2_fp4_m{m}", dict(GEMV_CFG, m=m), copies=16, steps=max(20, min(args.steps, 100)))
+
+    # one c5 layer's four projections (fused qkv, o, fused gate|up, down) at M=2048, bf16
+    cfg5 = S.C5
+    layer = {p: S.make_matrix(cfg5, 0, p, device, seed=3 + rank) for p in cfg5.proj_shapes()}
+    sh = S.shard_layer(layer, cfg5, 0, 1)
+    m5 = 2048
+    xs = {k: torch.randn((m5, w.shape[1]), device=device).to(torch.bfloat16) for k, w in
+          (("qkv", sh.qkv), ("o", sh.o), ("gu", sh.gu), ("down", sh.down))}
+    ys = {k: torch.empty((m5, w.shape[0]), device=device, dtype=torch.bfloat16) for k, w in
+          (("qkv", sh.qkv), ("o", sh.o), ("gu", sh.gu), ("down", sh.down))}
+    ws5 = {"qkv": sh.qkv, "o": sh.o, "gu": sh.gu, "down": sh.down}
+    d5 = {k: w.desc() for k, w in ws5.items()}
+    bf = _lib.DT["bfloat16"]
+
+    def launch5(i, stream):
+        for k, w in ws5.items():
+            rc = fn(ctypes.byref(d5[k]), xs[k].data_ptr(), bf, m5, w.shape[1], 1, ys[k].data_ptr(), bf, w.shape[0], 1, 0,
+                    stream)
+            if rc:
+                raise RuntimeError(_lib.last_error())
+
+    ms = max_ms(_graph_time_ms(launch5, 5, device))
+    flops = sum(2 * m5 * w.shape[0] * w.shape[1] for w in ws5.values())
+    tf = flops / (ms / 1e3) / 1e12
+    out["c5_layer_m2048"] = {"ms_per_layer": round(ms, 3), "TFLOP/s": round(tf, 1),
+                             "frac_of_tensor_peak": round(tf / peaks["bf16_tflops_sustained"], 4),
+                             "peak": "bf16_tflops_sustained (long loop)", "kernel": linear_plan(sh.gu, torch.bfloat16, m5,
+                                                                                              torch.bfloat16),
+                             "flops_per_layer": flops,
+                             "note": "weights of one layer stay in L2 between the 5 graph launches"}
+    del layer, sh, ws5, xs, ys
+
+    # c4 INT4 stack, one token through 32 layers on this GPU (no tensor parallelism)
+    st = S.TPStack(S.C4, 0, 1, device=device, seed=5 + rank)
+    h0 = torch.randn((1, S.C4.hidden), device=device).to(S.C4.act)
+    h = h0.clone()
+
+    def launch4(i, stream):
+        h.copy_(h0)
+        st.forward(h)
+
+    ms = max_ms(_graph_time_ms(launch4, 5, device))
+    total = S.C4.layer_weight_bytes() * S.C4.layers
+    out["c4_stack_m1"] = {"ms_per_token": round(ms, 3), "weight_gbs": round(total / (ms / 1e3) / 1e9, 1),
+                          "frac_of_hbm": round(total / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+                          "weight_bytes_per_token": total, "layers": S.C4.layers,
+                          "note": "INT4 group-128 fp16 scales; one GPU"}
+    del st
+    return out
 
 
 def run_gemm(args, device, world, rank):
@@ -465,7 +596,8 @@ def cpu_baseline(nthreads: int, budget_s: float) -> dict:
 def profile_case(case: str, launches: int):
     """Small untimed workload for ncu captures: `launches` plain b200_packed_linear calls.
 
-    gemv: c2 M=1 over 4 resident weight copies (143 MB > L2); gemm: c3 M=4096 (one weight).
+    gemv: c2 M=1 over 4 resident weight copies (143 MB > L2); skinny: the same at M=8;
+    gemm: c3 M=4096 (one weight).
     Nothing is timed; the process only has to exit 0 so the same command line can be profiled.
     """
     import torch
@@ -473,9 +605,11 @@ def profile_case(case: str, launches: int):
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    cfg = dict(GEMV_CFG if case == "gemv" else GEMM_CFG)
+    cfg = dict(GEMV_CFG if case in ("gemv", "skinny") else GEMM_CFG)
+    if case == "skinny":
+        cfg["m"] = 8
     xdt = getattr(torch, cfg["xdt"])
-    ws = make_weights(cfg, device, 4 if case == "gemv" else 1, seed=0)
+    ws = make_weights(cfg, device, 1 if case == "gemm" else 4, seed=0)
     x = (torch.randn((cfg["m"], cfg["k"]), device=device) / 8).to(xdt)
     y = torch.empty((cfg["m"], cfg["n"]), device=device, dtype=xdt)
     code = _lib.DT[cfg["xdt"]]
@@ -498,9 +632,10 @@ def main():
     ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--no-stack", action="store_true", help="skip the c5 layer-stack leg")
+    ap.add_argument("--no-configs", action="store_true", help="skip the c1 / c2 M=8,32 / c5 M=2048 / c4 legs")
     ap.add_argument("--stack-layers", type=int, default=None, help="layers of the c5 stack leg (default: all 80)")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
-    ap.add_argument("--profile-case", choices=["gemv", "gemm"], default=None,
+    ap.add_argument("--profile-case", choices=["gemv", "skinny", "gemm"], default=None,
                     help="run a small untimed workload for ncu and exit")
     ap.add_argument("--launches", type=int, default=6, help="launches of --profile-case")
     args = ap.parse_args()
