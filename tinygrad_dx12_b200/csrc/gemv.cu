@@ -239,10 +239,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       prefetch_tmap(&tmw);
       if constexpr (GROUP) prefetch_tmap(&tms);
       int64_t gs = 0;
+      int slot = 0;        // gs % STAGES, kept incrementally (no 64-bit division in the loop)
+      uint32_t round = 0;  // (gs / STAGES) & 1
       for (int64_t rbk = rb_begin; rbk < rb_end; ++rbk) {
-        for (int st = 0; st < sp.nst; ++st, ++gs) {
-          const int slot = (int)(gs % STAGES);
-          if (gs >= STAGES && !mbar_wait(&empty[slot], (uint32_t)((gs / STAGES - 1) & 1), abort_flag)) continue;
+        for (int st = 0; st < sp.nst; ++st, ++gs, (++slot == STAGES ? (slot = 0, round ^= 1u) : 0u)) {
+          if (gs >= STAGES && !mbar_wait(&empty[slot], round ^ 1u, abort_flag)) continue;
           if (*abort_flag) continue;
           uint8_t *dst = ring + slot * SLOT;
           mbar_arrive_expect_tx(&full[slot], TX);
@@ -293,14 +294,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int bm = g >> 2;
   const bool owner = (t == (g & 3)) && bm < p.m;
   const __half *xrow = xs + (int64_t)bm * K + 32 * t;
-  int64_t gs = 0;
+  int slot = 0;        // ring slot of the current stage, kept incrementally
+  uint32_t round = 0;  // its phase parity
   int buf = 0;
   for (int64_t rbk = rb_begin; rbk < rb_end; ++rbk) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, g+16, g+24 for m = cm
-    for (int st = 0; st < sp.nst; ++st, ++gs) {
+    for (int st = 0; st < sp.nst; ++st, (++slot == STAGES ? (slot = 0, round ^= 1u) : 0u)) {
       if ((st & 1) != parity) continue;
-      const int slot = (int)(gs % STAGES);
-      const bool got = mbar_wait(&full[slot], (uint32_t)((gs / STAGES) & 1), abort_flag);
+      const bool got = mbar_wait(&full[slot], round, abort_flag);
       const uint8_t *base = ring + slot * SLOT;
       Chunk4<BITS> r;
       if (got) {
