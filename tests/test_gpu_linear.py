@@ -161,3 +161,14 @@ def test_e8m0_special_bytes(m):
     assert_close(y[:, 1:], r[:, 1:], "float32")
     y0, r0 = y[:, 0].astype(np.float64) * 2.0**127, r[:, 0].astype(np.float64) * 2.0**127
     assert np.all(np.abs(y0 - r0) <= 1e-3 * np.maximum(np.abs(r0), 1.0))
+
+
+@pytest.mark.parametrize("bs", [64, 128, 256, 512])
+@pytest.mark.parametrize("scale", ["float16", "bfloat16", "float32"])
+@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("fmt", ["int4", "fp6_e3m2"])
+def test_group_scales_decode_gemv(bs, scale, m, fmt):
+    """Group scales wider than one 32-payload block (c4 uses 128) on the decode GEMV."""
+    spec = _spec(fmt, 320, 2048, bs, "f16u", 31)
+    plan, *_ = _run(spec, scale, m, "float16", "float16", "gemv")
+    assert plan == "gemv"
