@@ -114,9 +114,9 @@ int32_t launch_gate_mul(const void *gu, int gdt, void *out, int odt, int64_t M, 
 // Each rank's row-parallel projection has written its fp32 partial (M x H) into its own buffer,
 // which every peer has mapped (CUDA IPC). For row r, CTA r:
 //   1. e = ++epoch[r] (this rank's count of reductions of row r; the same on every rank);
-//   2. publishes e in flags[rank][r] of every rank (release, system scope);
-//   3. waits until flags[q][r] >= e locally for every rank q (bounded; on give-up it flags the
-//      device error word and continues);
+//   2. publishes e in flags[rank][r] of every rank and 3. waits until flags[q][r] >= e locally
+//      for every rank q -- thread q talks to rank q, with a system-scope fence before its store
+//      and after its last load (bounded; on give-up it flags the device error word and continues);
 //   4. sums the partial rows of ranks 0..world-1 in that order (identical on every rank, so h
 //      stays bitwise replicated), adds the sum to h and writes x = rmsnorm(h).
 // A rank reuses a partial buffer only two reductions later, after every peer has signalled
@@ -141,12 +141,12 @@ struct PeerReduce {
   int64_t timeout_ns;
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t *p) {
   uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -168,22 +168,28 @@ __global__ void __launch_bounds__(PR_THREADS) peer_reduce_rmsnorm_kernel(PeerRed
   __shared__ float red[PR_THREADS / 32 + 1];
   const int64_t row = blockIdx.x;
   pdl_enter();  // this rank's partial is complete from here on
+  __shared__ uint32_t e_sh;
   if (threadIdx.x == 0) {
-    const uint32_t e = pr.epoch[row] + 1u;
-    pr.epoch[row] = e;
-    __threadfence_system();  // this rank's partial (written by the previous kernel) before the flags
-    for (int q = 0; q < pr.world; ++q) st_release_sys(pr.flags[q] + (int64_t)pr.rank * pr.rows_max + row, e);
-    const uint32_t *mine = pr.flags[pr.rank];
+    e_sh = pr.epoch[row] + 1u;
+    pr.epoch[row] = e_sh;
+  }
+  __syncthreads();
+  const uint32_t e = e_sh;
+  if (threadIdx.x < pr.world) {
+    // thread q signals rank q and waits for rank q's signal: one NVLink round trip overall
+    const int q = threadIdx.x;
+    asm volatile("fence.acq_rel.sys;" ::: "memory");  // the partial is visible before the flag
+    st_relaxed_sys(pr.flags[q] + (int64_t)pr.rank * pr.rows_max + row, e);
+    const uint32_t *f = pr.flags[pr.rank] + (int64_t)q * pr.rows_max + row;
     const uint64_t t0 = globaltimer();
-    for (int q = 0; q < pr.world; ++q) {
-      for (uint32_t i = 0;; ++i) {
-        if ((int32_t)(ld_acquire_sys(mine + (int64_t)q * pr.rows_max + row) - e) >= 0) break;
-        if ((i & 255u) == 255u && globaltimer() - t0 > (uint64_t)pr.timeout_ns) {
-          atomicOr(&g_device_error, B200_DEVERR_MBAR_TIMEOUT);
-          break;
-        }
+    for (uint32_t i = 0;; ++i) {
+      if ((int32_t)(ld_relaxed_sys(f) - e) >= 0) break;
+      if ((i & 255u) == 255u && globaltimer() - t0 > (uint64_t)pr.timeout_ns) {
+        atomicOr(&g_device_error, B200_DEVERR_MBAR_TIMEOUT);
+        break;
       }
     }
+    asm volatile("fence.acq_rel.sys;" ::: "memory");  // rank q's partial is read after its flag
   }
   __syncthreads();
   T *hr = h + row * H;

@@ -312,8 +312,11 @@ class TPStack:
         x = torch.empty_like(h)
         mbuf = torch.empty((m, self.layers[0].inter_rows if self.layers else 0), dtype=cfg.act, device=h.device)
         ops.add_rmsnorm(h, None, x)
-        row_reduce = getattr(ops, "row_reduce", None) or (lambda w, inp, hh, xx, slot: _generic_row_reduce(ops, w, inp,
-                                                                                                           hh, xx))
+        if self.world == 1:  # unsharded: nothing to reduce whatever the process group holds
+            row_reduce = lambda w, inp, hh, xx, slot: _local_row_reduce(ops, w, inp, hh, xx)  # noqa: E731
+        else:
+            row_reduce = getattr(ops, "row_reduce", None) or (
+                lambda w, inp, hh, xx, slot: _generic_row_reduce(ops, w, inp, hh, xx))
         for L in self.layers:
             qkv = ops.linear(L.qkv, x, cfg.act)
             row_reduce(L.o, qkv[:, :L.q_rows], h, x, 0)
@@ -321,6 +324,10 @@ class TPStack:
             ops.gate_mul(gu, mbuf)
             row_reduce(L.down, mbuf, h, x, 1)
         return h
+
+
+def _local_row_reduce(ops, w, inp, h, x) -> None:
+    ops.add_rmsnorm(h, ops.linear(w, inp, torch.float32), x)
 
 
 def _generic_row_reduce(ops, w, inp, h, x) -> None:
