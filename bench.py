@@ -244,6 +244,38 @@ def run_gpu_arm(args, world, rank, local):
         dist.all_reduce(ems, op=dist.ReduceOp.MAX)
     e2e_value = bytes_step * e_steps * world / (float(ems.item()) / 1e3) / 1e9
 
+    # the same public-API step replayed from a CUDA graph (how a TinyJit decode loop runs it):
+    # H2D of x from pinned memory, tg.matmul, D2H of y into pinned memory, every step
+    gstream = torch.cuda.Stream(device)
+    xg = torch.empty((cfg["m"], cfg["k"]), device=device, dtype=xdt)
+    g_steps = max(10, min(args.steps, 100))
+    with torch.cuda.stream(gstream):
+        for i in range(3):
+            xg.copy_(xh, non_blocking=True)
+            yh.copy_(tg.matmul(ws[i % copies], xg.t(), dtype=xdt).t(), non_blocking=True)
+    torch.cuda.synchronize()
+    e2e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(e2e_graph, stream=gstream):
+        for i in range(g_steps):
+            xg.copy_(xh, non_blocking=True)
+            yh.copy_(tg.matmul(ws[i % copies], xg.t(), dtype=xdt).t(), non_blocking=True)
+    with torch.cuda.stream(gstream):
+        e2e_graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(gstream):
+        g0.record(gstream)
+        e2e_graph.replay()
+        g1.record(gstream)
+    torch.cuda.synchronize()
+    del e2e_graph
+    gms = torch.tensor([g0.elapsed_time(g1)], device=device)
+    if world > 1:
+        dist.all_reduce(gms, op=dist.ReduceOp.MAX)
+    e2e_graph_value = bytes_step * g_steps * world / (float(gms.item()) / 1e3) / 1e9
+
     gemm = None
     if not args.no_gemm:
         gemm = run_gemm(args, device, world, rank)
@@ -284,7 +316,10 @@ def run_gpu_arm(args, world, rank, local):
                          "algorithmic_bytes_per_launch": bytes_step},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": cfg["m"] * cfg["k"] * 2, "d2h_bytes_per_step": cfg["m"] * cfg["n"] * 2,
-                    "path": "tinygrad_dx12_b200.matmul(W, x.T, dtype=bf16) with pinned-host x in and y out"},
+                    "path": "tinygrad_dx12_b200.matmul(W, x.T, dtype=bf16) with pinned-host x in and y out, "
+                            "eager Python calls",
+                    "graph_value": round(e2e_graph_value, 2),
+                    "graph_path": "the same H2D + tg.matmul + D2H step replayed from a CUDA graph"},
             "gpu_launches": args.steps,
             "clocks": clk.summary(),
         }

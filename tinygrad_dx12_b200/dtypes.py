@@ -10,6 +10,8 @@ promoted like float32: every E8M0 value is exactly a float32 power of two.
 
 from __future__ import annotations
 
+import functools
+
 import torch
 
 NAMES = {
@@ -57,6 +59,7 @@ def _upper(n: str) -> set[str]:
     return out
 
 
+@functools.lru_cache(maxsize=1024)
 def least_upper_dtype(*dts: torch.dtype) -> torch.dtype:
     common = set.intersection(*(_upper(name(d)) for d in dts))
     return TORCH[min(common, key=_PRIORITY.__getitem__)]
@@ -70,6 +73,7 @@ def is_unsigned(dt: torch.dtype) -> bool:
     return name(dt) in ("uint8", "uint16", "uint32", "uint64")
 
 
+@functools.lru_cache(maxsize=256)
 def sum_acc_dtype(dt: torch.dtype) -> torch.dtype:
     if is_unsigned(dt):
         return least_upper_dtype(dt, torch.uint32)
@@ -78,6 +82,7 @@ def sum_acc_dtype(dt: torch.dtype) -> torch.dtype:
     return least_upper_dtype(dt, torch.float32)
 
 
+@functools.lru_cache(maxsize=256)
 def accumulator(a: torch.dtype, b: torch.dtype) -> torch.dtype:
     """renderer/linalg.py:33-35."""
     return sum_acc_dtype(least_upper_dtype(a, b))

@@ -165,9 +165,16 @@ def matmul(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor, scope
         fused = _fused_operands(a, b, out_dtype)
         if fused is not None:
             w, x = fused
-            for path in _SCOPE_PATHS[scope]:
-                if linear_plan(w, x.dtype, x.shape[0], out_dtype, path) is not None:
-                    return _packed_linear(w, x, out_dtype, path).t()
+            if automatic:  # one library call: it picks the kernel or reports that none fits
+                try:
+                    return _packed_linear(w, x, out_dtype, "auto").t()
+                except _lib.B200Error as error:
+                    if error.code != _lib.ERR_UNSUPPORTED:
+                        raise
+            else:
+                for path in _SCOPE_PATHS[scope]:
+                    if linear_plan(w, x.dtype, x.shape[0], out_dtype, path) is not None:
+                        return _packed_linear(w, x, out_dtype, path).t()
         if not automatic:
             raise RuntimeError(f"B200 {scope} {tile} rejected: no fused kernel for these operands")
     # ordinary compute: decode to the intermediate, then the generic matmul

@@ -10,6 +10,7 @@ There is no CPU path: a packed operand on any other device is rejected.
 
 from __future__ import annotations
 
+import functools
 import math
 from dataclasses import dataclass
 
@@ -90,8 +91,15 @@ class PackedTensor:
         return self.shape[-1]
 
     def desc(self) -> _lib.PackedDesc:
-        """The C-ABI descriptor (rows = prod(shape[:-1]), cols = shape[-1])."""
+        """The C-ABI descriptor (rows = prod(shape[:-1]), cols = shape[-1]).
+
+        Cached while ``data`` and ``scales`` are contiguous (the descriptor then holds only their
+        device addresses, which in-place updates keep)."""
+        cached = self.__dict__.get("_desc")
+        if cached is not None:
+            return cached
         _require_cuda(self.data, "packed data")
+        contiguous = self.data.is_contiguous() and (self.scales is None or self.scales.is_contiguous())
         data = self.data if self.data.is_contiguous() else self.data.contiguous()
         scales = None
         if self.scales is not None:
@@ -104,6 +112,8 @@ class PackedTensor:
         d.rows, d.cols, d.block_size = self.rows, self.cols, self.block_size
         d.scales = scales.data_ptr() if scales is not None and scales.numel() else None
         d._keep = (data, scales)  # keep contiguous copies alive for the call
+        if contiguous:
+            object.__setattr__(self, "_desc", d)
         return d
 
     def default_dtype(self) -> torch.dtype:
@@ -144,22 +154,39 @@ def ctypes_ref(d: _lib.PackedDesc):
     return ctypes.byref(d)
 
 
+def _operand_key(op):
+    """What matrix_intermediate depends on: a dtype, or a packed format and its scale dtype."""
+    if isinstance(op, PackedTensor):
+        return ("packed", op.format, None if op.scales is None else op.scales.dtype)
+    return ("tensor", op.dtype)
+
+
+@functools.lru_cache(maxsize=512)
+def _intermediate_for(ka, kb) -> torch.dtype:
+    cands, declared = [], []
+    for k in (ka, kb):
+        if k[0] == "tensor":
+            cands.append({k[1]})
+            declared.append(k[1])
+        else:
+            _, fmt, sdt = k
+            cands.append(set(FP8_CANDIDATES.get(fmt, ())) if sdt is None else set())
+            declared.append(D.least_upper_dtype(torch.float32, sdt) if sdt is not None else
+                            {"int4": torch.int8, "uint4": torch.uint8}.get(fmt, torch.float16))
+    both = set.intersection(*cands)
+    for dt in (torch.float8_e4m3fn, torch.float8_e5m2):
+        if dt in both:
+            return dt
+    return D.least_upper_dtype(*declared)
+
+
 def matrix_intermediate(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor, native16: bool = False) -> torch.dtype:
     """Shared dtype promotion after selecting an exact packed storage representation (dx12.py:115-138).
 
     Prefer a common FP8 encoding when both operands fit; otherwise promote the declared
     types. ``native16`` is accepted for signature compatibility and changes nothing.
     """
-    operands = (a, b)
-    candidates = set.intersection(*[
-        {op.dtype} if isinstance(op, torch.Tensor)
-        else set(FP8_CANDIDATES.get(op.format, ())) if op.scales is None else set()
-        for op in operands
-    ])
-    for dt in (torch.float8_e4m3fn, torch.float8_e5m2):
-        if dt in candidates:
-            return dt
-    return D.least_upper_dtype(*[op.dtype for op in operands])
+    return _intermediate_for(_operand_key(a), _operand_key(b))
 
 
 def matmul(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor) -> torch.Tensor:
