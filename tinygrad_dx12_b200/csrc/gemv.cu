@@ -330,15 +330,6 @@ __global__ void __launch_bounds__(THREADS, 1)
             r.hi.sa0 = __uint_as_float((u2 & 0xFFu) << 23), r.hi.sa1 = __uint_as_float((u2 & 0xFF00u) << 15);
             r.hi.sb0 = __uint_as_float((u3 & 0xFFu) << 23), r.hi.sb1 = __uint_as_float((u3 & 0xFF00u) << 15);
           }
-        } else if constexpr (SK == SK_GROUP) {
-          // group scales (block 64..512, a multiple of this lane's two 32-blocks): one scale per row
-          const int64_t gi = ((int64_t)st * KSTAGE + (int64_t)sub * CHUNK + 32 * cblk) / p.block;
-          const int64_t r0 = rbk * RB + g;
-          const float s0 = r0 < p.rows ? load_as_f32(p.scales, r0 * p.nblk + gi, p.sdt) : 0.f;
-          const float s1 = r0 + 8 < p.rows ? load_as_f32(p.scales, (r0 + 8) * p.nblk + gi, p.sdt) : 0.f;
-          const float s2 = r0 + 16 < p.rows ? load_as_f32(p.scales, (r0 + 16) * p.nblk + gi, p.sdt) : 0.f;
-          const float s3 = r0 + 24 < p.rows ? load_as_f32(p.scales, (r0 + 24) * p.nblk + gi, p.sdt) : 0.f;
-          r.lo.sa0 = r.lo.sa1 = s0, r.lo.sb0 = r.lo.sb1 = s1, r.hi.sa0 = r.hi.sa1 = s2, r.hi.sb0 = r.hi.sb1 = s3;
         } else if constexpr (GROUP) {
           const uint8_t *sb = base + RB * WR;
           const int blk = sub * 4 + cblk;  // block index within the stage's 16 blocks per row
@@ -453,7 +444,6 @@ static int32_t dispatch_sk(const LinearArgs &a, int sk, cudaStream_t stream) {
     case SK_F16: return launch_t<FMT, SK_F16>(a, stream);
     case SK_BF16: return launch_t<FMT, SK_BF16>(a, stream);
     case SK_F32: return launch_t<FMT, SK_F32>(a, stream);
-    case SK_GROUP: return launch_t<FMT, SK_GROUP>(a, stream);
   }
   return b200_set_error(B200_ERR_UNSUPPORTED, "streamed GEMV: scale layout");
 }
@@ -465,9 +455,9 @@ bool gemv_stream_supported(const LinearArgs &a) {
   if (!gemv_tc_supported(a)) return false;
   if (a.cols % KSTAGE != 0 || a.cols > (1 << 24)) return false;
   const int sk = gemv::scale_kind(a);
-  // group scales wider than 32 (block 64..512) are handled by the kernel below (one global scale
-  // load per row and chunk) but measured slower than the register-ring GEMV, which prefetches
-  // them with the weights (c4 stack: 4.7 vs 2.6 ms per token): leave them to that kernel
+  // group scales wider than 32 (block 64..512) go to the register-ring GEMV, which prefetches
+  // them with the weights (a variant of this kernel loading one scale per row and chunk from
+  // global memory measured slower: c4 stack 4.7 vs 2.6 ms per token)
   if (sk == gemv::SK_GROUP) return false;
   if (sk >= gemv::SK_E8M0) {
     const int esz = dt_size(a.sdt);
