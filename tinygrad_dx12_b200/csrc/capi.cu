@@ -288,10 +288,11 @@ int32_t b200_device_status(int32_t device, uint32_t *flags, int32_t clear) {
   unsigned int v = 0, u = 0;
   if (int32_t rc = gemm_device_error(&v, clear != 0)) return rc;
   if (int32_t rc = gemv_device_error(&u, clear != 0)) return rc;
-  unsigned int w = 0, z = 0;
+  unsigned int w = 0, z = 0, dd = 0;
   if (int32_t rc = skinny_device_error(&w, clear != 0)) return rc;
   if (int32_t rc = stackops_device_error(&z, clear != 0)) return rc;
-  *flags = v | u | w | z;
+  if (int32_t rc = gemm_dense_device_error(&dd, clear != 0)) return rc;
+  *flags = v | u | w | z | dd;
   return B200_OK;
 }
 

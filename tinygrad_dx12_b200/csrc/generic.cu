@@ -1,7 +1,8 @@
 // generic.cu -- ordinary kernels the packed path still needs around the fused kernels:
 //   * matmul_generic: the "tiled" scope (tinygrad-dx12 src/tinygrad_dx12/codegen/linalg.py:188-189,
-//     ordinary compute) for integer / float64 / mixed cases the fused kernels do not take,
-//     e.g. packed integer weights times int32/int64 activations (test_linalg.py:202-218);
+//     ordinary compute). fp16 / bf16 operands in tensor-core layouts go to the tcgen05 dense GEMM
+//     (gemm_dense.cu); everything else -- integer / float64 / mixed cases, e.g. packed integer
+//     weights times int32/int64 activations (test_linalg.py:202-218) -- runs the tiled kernel here;
 //   * cast: elementwise numeric conversion (the `.cast()` nodes of linalg.py:180-181);
 //   * wait_flag: a bounded device-side wait that reports a timeout instead of hanging.
 #include "common.cuh"
@@ -50,6 +51,9 @@ int32_t launch_matmul_generic(const void *a, int adt, int64_t sam, int64_t sak, 
                               int64_t sbn, void *c, int cdt, int64_t scm, int64_t scn, int64_t M, int64_t N, int64_t K,
                               int accdt, cudaStream_t stream) {
   if (M <= 0 || N <= 0) return B200_OK;
+  // 16-bit operands in tensor-core layouts: the tcgen05 GEMM (fp32 accumulation, as below)
+  if (gemm_dense_supported(a, adt, sam, sak, b, bdt, sbk, sbn, cdt, scn, M, N, K, accdt))
+    return launch_gemm_dense(a, adt, sam, b, sbn, c, cdt, scm, M, N, K, stream);
   const dim3 grid((unsigned)((N + 15) / 16), (unsigned)((M + 15) / 16));
   if (grid.y > 65535u) return b200_set_error(B200_ERR_UNSUPPORTED, "generic matmul: M=%lld too large", (long long)M);
   switch (accdt) {

@@ -56,6 +56,14 @@ int32_t skinny_device_error(unsigned int *v, bool clear);
 // same kernel, split-K scratch from a fixed device array instead of a library workspace
 int32_t launch_skinny_noalloc(const LinearArgs &a, cudaStream_t stream);
 
+// dense fp16 / bf16 tcgen05 GEMM for ordinary matmuls (gemm_dense.cu): c = a @ b with a
+// row-major (k contiguous) and b K-major (k contiguous per column), fp32 accumulation
+bool gemm_dense_supported(const void *a, int adt, int64_t sam, int64_t sak, const void *b, int bdt, int64_t sbk,
+                          int64_t sbn, int cdt, int64_t scn, int64_t M, int64_t N, int64_t K, int accdt);
+int32_t launch_gemm_dense(const void *a, int adt, int64_t sam, const void *b, int64_t sbn, void *c, int cdt,
+                          int64_t scm, int64_t M, int64_t N, int64_t K, cudaStream_t stream);
+int32_t gemm_dense_device_error(unsigned int *v, bool clear);
+
 int32_t launch_matmul_generic(const void *a, int adt, int64_t sam, int64_t sak, const void *b, int bdt, int64_t sbk,
                               int64_t sbn, void *c, int cdt, int64_t scm, int64_t scn, int64_t M, int64_t N, int64_t K,
                               int accdt, cudaStream_t stream);

@@ -42,8 +42,28 @@ def _check_cuda(device: torch.device) -> None:
         raise ValueError(f"the B200 matrix API requires CUDA tensors (got device {device})")
 
 
+DENSE_IO = (torch.float16, torch.bfloat16)
+
+
+def _tensor_core_layout(lhs: torch.Tensor, rhs: torch.Tensor, out_dtype: torch.dtype):
+    """16-bit operands for the tcgen05 dense GEMM: lhs row-major, rhs K-major (columns with k
+    contiguous), both 16-byte aligned; copies an operand only when its layout does not fit."""
+    if lhs.dtype != rhs.dtype or lhs.dtype not in DENSE_IO or out_dtype not in FUSED_IO:
+        return lhs, rhs
+    m, k = lhs.shape
+    if k % 8 or k < 16 or m * rhs.shape[1] * k < (1 << 18):
+        return lhs, rhs  # tiny or unaligned: the tiled kernel
+    if lhs.stride(1) != 1 or lhs.stride(0) % 8 or lhs.data_ptr() % 16:
+        lhs = lhs.contiguous()
+    if rhs.stride(0) != 1 or rhs.stride(1) % 8 or rhs.data_ptr() % 16:
+        rhs = rhs.t().contiguous().t()
+    return lhs, rhs
+
+
 def _generic_matmul(lhs: torch.Tensor, rhs: torch.Tensor, out_dtype: torch.dtype, acc_dtype: torch.dtype) -> torch.Tensor:
-    """Ordinary matmul through ``b200_matmul_generic`` (linalg.py:188-189, the 'tiled' scope)."""
+    """Ordinary matmul through ``b200_matmul_generic`` (linalg.py:188-189, the 'tiled' scope);
+    16-bit operands run on the tcgen05 dense GEMM."""
+    lhs, rhs = _tensor_core_layout(lhs, rhs, out_dtype)
     m, k = lhs.shape
     n = rhs.shape[1]
     fp8_out = out_dtype in (torch.float8_e4m3fn, torch.float8_e5m2)
