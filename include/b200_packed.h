@@ -175,6 +175,14 @@ int32_t b200_device_status(int32_t device, uint32_t *flags, int32_t clear);
 int32_t b200_device_wait_flag(const int32_t *flag, int32_t expect, int64_t max_spins, int32_t *status,
                               void *stream);
 
+/* b200_packed_linear (path AUTO, unit k / n strides) writing the same result to n_y <= 8
+ * destinations of one layout -- e.g. this rank's slot in every rank's peer-mapped buffer, the
+ * push half of the tensor-parallel reduction. The decode GEMV (m <= 2) stores every destination
+ * from its epilogue; other kernels compute into y[0] and copy. No counterpart in the reference. */
+int32_t b200_packed_linear_multi(const b200_packed_desc *w, const void *x, int32_t x_dtype, int64_t m,
+                                 int64_t x_stride_m, void *const *y, int32_t n_y, int32_t y_dtype, int64_t y_stride_m,
+                                 int32_t flags, void *stream);
+
 /* Allocation-free form of b200_packed_linear for a few tokens (3 <= m <= 32, 4-bit formats,
  * the split-K decode GEMM). No counterpart in the reference. Same arguments and result as
  * b200_packed_linear with path B200_PATH_GEMV and unit k / n strides; bitwise the same result.

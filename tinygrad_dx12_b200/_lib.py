@@ -68,6 +68,7 @@ SIGNATURES = {
     "b200_event_elapsed_ms": ([_P, _P, ctypes.POINTER(ctypes.c_float)], _I32),
     "b200_event_destroy": ([_P], _I32),
     "b200_device_wait_flag": ([_P, _I32, _I64, _P, _P], _I32),
+    "b200_packed_linear_multi": ([_DESC, _P, _I32, _I64, _I64, _P, _I32, _I32, _I64, _I32, _P], _I32),
     "b200_packed_linear_noalloc": ([_DESC, _P, _I32, _I64, _I64, _P, _I32, _I64, _P], _I32),
     "b200_peer_allreduce_add_rmsnorm": ([_P, _P, _P, _I32, _I32, _I64, _I64, _P, _I32, _P, _I32, _I64, _I64,
                                          ctypes.c_float, _P], _I32),

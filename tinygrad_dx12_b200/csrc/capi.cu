@@ -127,6 +127,8 @@ static bool fill_linear(const b200_packed_desc *w, const void *x, int32_t x_dtyp
   a.ldy_m = y_stride_m;
   a.ldy_n = y_stride_n;
   a.flags = 0;
+  a.ncopy = 0;
+  for (int i = 0; i < 7; ++i) a.ycopy[i] = nullptr;
   return x_stride_k == 1;
 }
 
@@ -293,6 +295,40 @@ int32_t b200_device_status(int32_t device, uint32_t *flags, int32_t clear) {
   if (int32_t rc = stackops_device_error(&z, clear != 0)) return rc;
   if (int32_t rc = gemm_dense_device_error(&dd, clear != 0)) return rc;
   *flags = v | u | w | z | dd;
+  return B200_OK;
+}
+
+int32_t b200_packed_linear_multi(const b200_packed_desc *w, const void *x, int32_t x_dtype, int64_t m,
+                                 int64_t x_stride_m, void *const *y, int32_t n_y, int32_t y_dtype, int64_t y_stride_m,
+                                 int32_t flags, void *stream) {
+  if (int32_t rc = injected()) return rc;
+  if (int32_t rc = validate_desc(w)) return rc;
+  if (m < 0 || n_y < 1 || n_y > 8 || y == nullptr) return b200_set_error(B200_ERR_INVALID, "bad m or destinations");
+  for (int i = 0; i < n_y; ++i)
+    if (y[i] == nullptr) return b200_set_error(B200_ERR_INVALID, "null destination %d", i);
+  if (m == 0 || w->rows == 0) return B200_OK;
+  if (x == nullptr) return b200_set_error(B200_ERR_INVALID, "null x");
+  LinearArgs a;
+  const bool ks = fill_linear(w, x, x_dtype, m, x_stride_m, 1, y[0], y_dtype, y_stride_m, 1, a);
+  a.flags = flags & ~0xFF;
+  const int32_t p = plan(a, ks, B200_PATH_AUTO);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (p == B200_PATH_GEMV && a.m <= 2) {  // the decode GEMV epilogue writes every destination
+    a.ncopy = n_y - 1;
+    for (int i = 1; i < n_y; ++i) a.ycopy[i - 1] = y[i];
+    return gemv_stream_supported(a) ? launch_gemv_stream(a, s) : launch_gemv_tc(a, s);
+  }
+  int32_t rc = B200_ERR_UNSUPPORTED;
+  switch (p) {
+    case B200_PATH_GEMV: rc = launch_skinny(a, s); break;
+    case B200_PATH_GEMM: rc = launch_gemm(a, s); break;
+    case B200_PATH_SIMT: rc = launch_gemv_simt(a, s); break;
+    default: return b200_set_error(B200_ERR_UNSUPPORTED, "no fused kernel for these operands");
+  }
+  if (rc != B200_OK) return rc;
+  const size_t row_bytes = (size_t)w->rows * dt_size(y_dtype), pitch = (size_t)y_stride_m * dt_size(y_dtype);
+  for (int i = 1; i < n_y; ++i)
+    B200_CUDA_TRY(cudaMemcpy2DAsync(y[i], pitch, y[0], pitch, row_bytes, (size_t)m, cudaMemcpyDeviceToDevice, s));
   return B200_OK;
 }
 

@@ -365,6 +365,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         s *= place_factor<FMT>() / prescale;
         if constexpr (SK == SK_ROW) s *= load_as_f32(p.scales, n * p.nblk, p.sdt);
         store_f32(p.y, mm * p.ldy_m + n * p.ldy_n, p.ydt, s);
+        for (int i = 0; i < p.ncopy; ++i) store_f32(p.ycopy[i], mm * p.ldy_m + n * p.ldy_n, p.ydt, s);
       }
     }
     buf ^= 1;
@@ -416,6 +417,8 @@ static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
   p.w = a.w, p.scales = a.scales, p.sdt = a.sdt, p.rows = a.rows, p.cols = a.cols, p.nblk = a.nblk, p.block = a.block;
   p.x = a.x, p.m = a.m, p.ldx = a.m > 1 ? a.ldx : a.cols, p.y = a.y, p.ydt = a.ydt, p.ldy_m = a.ldy_m,
   p.ldy_n = a.ldy_n, p.pdl = 0;
+  p.ncopy = a.ncopy;
+  for (int i = 0; i < 7; ++i) p.ycopy[i] = i < a.ncopy ? a.ycopy[i] : nullptr;
   sp.nrb = (a.rows + RB - 1) / RB;
   sp.nst = (int)(a.cols / KSTAGE);
   sp.xbf16 = a.xdt == B200_DT_BF16;

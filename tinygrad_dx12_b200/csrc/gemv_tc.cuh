@@ -44,6 +44,8 @@ struct Params {
   int ydt;
   int64_t ldy_m, ldy_n;
   int pdl;  // launched with programmatic stream serialization
+  void *ycopy[7];  // further destinations of y (same layout), e.g. peers' buffers
+  int ncopy;
 };
 
 
@@ -268,6 +270,7 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_bd_kernel(Params p, int xbf16
       s *= place_factor<FMT>() / prescale;
       if constexpr (SK == SK_ROW) s *= load_as_f32(p.scales, n * p.nblk, p.sdt);
       store_f32(p.y, mm * p.ldy_m + n * p.ldy_n, p.ydt, s);
+      for (int i = 0; i < p.ncopy; ++i) store_f32(p.ycopy[i], mm * p.ldy_m + n * p.ldy_n, p.ydt, s);
     }
   }
 }
@@ -364,6 +367,8 @@ int32_t launch_gemv_tc(const LinearArgs &a, cudaStream_t stream) {
   p.ldy_m = a.ldy_m;
   p.ldy_n = a.ldy_n;
   p.pdl = (a.flags & B200_FLAG_PDL) ? 1 : 0;
+  p.ncopy = a.ncopy;
+  for (int i = 0; i < 7; ++i) p.ycopy[i] = i < a.ncopy ? a.ycopy[i] : nullptr;
   const bool bf = a.xdt == B200_DT_BF16;
   const int sk = scale_kind(a);
   switch (a.fmt) {

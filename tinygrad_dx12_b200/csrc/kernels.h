@@ -22,6 +22,8 @@ struct LinearArgs {
   int ydt;
   int64_t ldy_m, ldy_n;
   int flags;  // B200_FLAG_* bits
+  void *ycopy[7];  // further destinations that receive the same y (decode GEMV epilogues)
+  int ncopy;
 };
 
 int32_t launch_dequant(const b200_packed_desc *w, int64_t begin, int64_t count, void *out, int32_t out_dtype,

@@ -122,15 +122,16 @@ def _packed_linear(w: PackedTensor, x: torch.Tensor, out_dtype: torch.dtype, pat
     return y
 
 
-def _packed_linear_into(w: PackedTensor, x: torch.Tensor, y_ptr: int, out_dtype: torch.dtype, ldy: int,
-                        path: str = "auto", flags: int = 0) -> None:
-    """Like ``_packed_linear`` but into caller-owned device memory (row-major, row pitch ``ldy``)."""
+def _packed_linear_multi(w: PackedTensor, x: torch.Tensor, y_ptrs, out_dtype: torch.dtype, ldy: int,
+                         flags: int = 0) -> None:
+    """``b200_packed_linear_multi``: the same y written to every address of ``y_ptrs`` (a ctypes
+    array of device pointers in this process, e.g. peer-mapped buffers), row pitch ``ldy``."""
     x = _aligned_x(x)
     m = x.shape[0]
     ldx = x.stride(0) if m > 1 else -(-x.shape[1] // 8) * 8
     d = w.desc()
-    _lib.call("b200_packed_linear", ctypes_ref(d), x.data_ptr(), _lib.DT[D.name(x.dtype)], m, ldx, 1, y_ptr,
-              _lib.DT[D.name(out_dtype)], ldy, 1, _lib.PATH[path] | flags, stream_ptr(x.device))
+    _lib.call("b200_packed_linear_multi", ctypes_ref(d), x.data_ptr(), _lib.DT[D.name(x.dtype)], m, ldx, y_ptrs,
+              len(y_ptrs), _lib.DT[D.name(out_dtype)], ldy, flags, stream_ptr(x.device))
 
 
 def linear_plan(w: PackedTensor, x_dtype: torch.dtype, m: int, out_dtype: torch.dtype, path: str = "auto") -> str | None:

@@ -196,9 +196,12 @@ class CudaOps:
 class PeerReducer:
     """Partial buffers shared by all ranks through CUDA IPC, and the fused one-shot reduction.
 
-    Per rank one device allocation holds two fp32 partial buffers (rows_max x hidden), the
-    flag words every rank writes into ([world][rows_max]) and this rank's epoch counters. The
-    allocation's IPC handle is exchanged over the process group; each rank maps every peer's.
+    Each rank owns one device allocation: fp32 partial slots [2][world][rows_max][hidden] (slot
+    [b][q] holds rank q's partial of reduction parity b), the flag words every rank writes
+    ([world][rows_max]) and this rank's epoch counters. The allocation's IPC handle is exchanged
+    over the process group and every rank maps every peer's. A rank's row-parallel projection
+    pushes its partial into slot [b][rank] of every rank (the GEMV epilogue stores to all of
+    them); the reduction then reads only local memory.
     """
 
     def __init__(self, rows_max: int, hidden: int, group=None, timeout_s: float = 5.0):
@@ -213,8 +216,9 @@ class PeerReducer:
         self.timeout_ns = int(timeout_s * 1e9)
         self.dev = torch.cuda.current_device()
         self.part_bytes = rows_max * hidden * 4
+        slots = 2 * self.world * self.part_bytes
         flag_bytes = self.world * rows_max * 4
-        total = 2 * self.part_bytes + flag_bytes + rows_max * 4
+        total = slots + flag_bytes + rows_max * 4
         base = ctypes.c_void_p()
         _lib.call("b200_malloc", self.dev, total, ctypes.byref(base))
         self.base = base.value
@@ -235,13 +239,21 @@ class PeerReducer:
             self.bases.append(p.value)
             self.opened.append(p.value)
         P = ctypes.c_void_p * 8
-        self._partials = [P(*[b + slot * self.part_bytes for b in self.bases]) for slot in (0, 1)]
-        self._flags = P(*[b + 2 * self.part_bytes for b in self.bases])
-        self.epoch = self.base + 2 * self.part_bytes + flag_bytes
+        w = self.world
+
+        def slot(base, b, src):
+            return base + (b * w + src) * self.part_bytes
+
+        order = [self.rank] + [q for q in range(w) if q != self.rank]  # local destination first
+        self._push = [(ctypes.c_void_p * w)(*[slot(self.bases[q], b, self.rank) for q in order]) for b in (0, 1)]
+        self._partials = [P(*[slot(self.base, b, q) for q in range(w)]) for b in (0, 1)]
+        self._flags = P(*[b_ + slots for b_ in self.bases])
+        self.epoch = self.base + slots + flag_bytes
         dist.barrier(group=group)  # every rank's flags are zero before anyone signals
 
-    def partial_ptr(self, slot: int) -> int:
-        return self.base + slot * self.part_bytes
+    def push_targets(self, slot: int):
+        """Where this rank's partial of reduction parity `slot` goes: its slot in every rank."""
+        return self._push[slot]
 
     def reduce(self, slot: int, h: torch.Tensor, x: torch.Tensor | None) -> None:
         m, hidden = h.shape
@@ -262,20 +274,20 @@ class PeerReducer:
 
 
 class PeerOps(CudaOps):
-    """CudaOps whose row-parallel projections write fp32 partials straight into the shared
-    buffers and reduce them with the fused peer-memory kernel (rows <= rows_max)."""
+    """CudaOps whose row-parallel projections push fp32 partials straight into every rank's
+    shared buffer and reduce them with the fused kernel (rows <= rows_max)."""
 
     def __init__(self, rows_max: int, hidden: int, group=None):
         super().__init__(group)
         self.reducer = PeerReducer(rows_max, hidden, group)
 
     def row_reduce(self, w: PackedTensor, inp: torch.Tensor, h: torch.Tensor, x: torch.Tensor, slot: int) -> None:
-        from .linalg import _packed_linear_into
+        from .linalg import _packed_linear_multi
 
         if h.shape[0] > self.reducer.rows_max:  # beyond the shared buffers: NCCL all-reduce
             return super().row_reduce(w, inp, h, x, slot)
-        _packed_linear_into(w, inp, self.reducer.partial_ptr(slot), torch.float32, h.shape[1], "auto",
-                            FLAG_PDL if inp.shape[0] <= 2 else 0)
+        _packed_linear_multi(w, inp, self.reducer.push_targets(slot), torch.float32, h.shape[1],
+                             FLAG_PDL if inp.shape[0] <= 2 else 0)
         self.reducer.reduce(slot, h, x)
 
     def close(self) -> None:
