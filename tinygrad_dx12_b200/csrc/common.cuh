@@ -16,6 +16,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/b200_packed.h"
 
 namespace b200 {
@@ -194,3 +196,39 @@ int32_t b200_set_error(int32_t code, const char *fmt, ...);
     if (_e != cudaSuccess) return b200_set_error(B200_ERR_CUDA, "kernel launch: %s (%s:%d)",   \
                                                  cudaGetErrorString(_e), __FILE__, __LINE__); \
   } while (0)
+
+namespace b200 {
+
+// Number of SMs of the current device (cached per device, thread-safe).
+inline cudaError_t device_sms(int *sms) {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  int v = cache[dev & 63].load(std::memory_order_relaxed);
+  if (v == 0) {
+    e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    cache[dev & 63].store(v, std::memory_order_relaxed);
+  }
+  *sms = v;
+  return cudaSuccess;
+}
+
+// Raise kernel K's dynamic shared-memory limit to `bytes` once per device (a per-function,
+// per-device setting; thread-safe, repeated calls are no-ops).
+template <auto K>
+inline cudaError_t ensure_dynamic_smem(int bytes) {
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+  return e;
+}
+
+}  // namespace b200
+

@@ -245,18 +245,12 @@ int32_t launch_gemm_dense(const void *a, int adt, int64_t sam, const void *b, in
                           int64_t scm, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
   using namespace dense;
   const bool bf = adt == B200_DT_BF16;
-  static bool attr[2] = {false, false};
-  static int sms = 0;
-  if (!attr[bf]) {
-    int dev = 0;
-    B200_CUDA_TRY(cudaGetDevice(&dev));
-    B200_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    if (bf)
-      B200_CUDA_TRY(cudaFuncSetAttribute(dense_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    else
-      B200_CUDA_TRY(cudaFuncSetAttribute(dense_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr[bf] = true;
-  }
+  int sms = 0;
+  B200_CUDA_TRY(device_sms(&sms));
+  if (bf)
+    B200_CUDA_TRY((ensure_dynamic_smem<dense_kernel<true>>(SMEM_BYTES)));
+  else
+    B200_CUDA_TRY((ensure_dynamic_smem<dense_kernel<false>>(SMEM_BYTES)));
   int bt = (int)((M + 31) / 32 * 32);
   if (bt > BT_MAX) bt = BT_MAX;
   const CUtensorMapDataType dt = bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;

@@ -395,15 +395,9 @@ namespace gemm {
 template <int FMT, bool BF16>
 static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
   constexpr int BITS = Fmt<FMT>::bits;
-  static bool attr_set = false;
-  static int sms = 0;
-  if (!attr_set) {
-    int dev = 0;
-    B200_CUDA_TRY(cudaGetDevice(&dev));
-    B200_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    B200_CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<FMT, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr_set = true;
-  }
+  int sms = 0;
+  B200_CUDA_TRY(device_sms(&sms));
+  B200_CUDA_TRY((ensure_dynamic_smem<gemm_kernel<FMT, BF16>>(SMEM_BYTES)));
   int bt = (int)((a.m + 31) / 32 * 32);
   if (bt > BT_MAX) bt = BT_MAX;
   const int ysz = a.ydt == B200_DT_F32 ? 4 : 2;

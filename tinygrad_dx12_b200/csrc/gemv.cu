@@ -382,17 +382,10 @@ template <int FMT, int SK>
 static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
   constexpr int BITS = Fmt<FMT>::bits;
   constexpr int SESZ = scale_esz<SK>();
-  static int sms = 0;
-  static bool attr = false;
   const size_t smem = smem_bytes<BITS, SESZ>(a.m, a.cols);
-  if (!attr) {
-    int dev = 0;
-    B200_CUDA_TRY(cudaGetDevice(&dev));
-    B200_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    B200_CUDA_TRY(cudaFuncSetAttribute(gemv_stream_kernel<FMT, SK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       200 * 1024));
-    attr = true;
-  }
+  int sms = 0;
+  B200_CUDA_TRY(device_sms(&sms));
+  B200_CUDA_TRY((ensure_dynamic_smem<gemv_stream_kernel<FMT, SK>>(200 * 1024)));
   int per_sm = 0;
   B200_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stream_kernel<FMT, SK>, THREADS, smem));
   if (per_sm < 1) return b200_set_error(B200_ERR_UNSUPPORTED, "streamed GEMV: no CTA fits (%zu B smem)", smem);

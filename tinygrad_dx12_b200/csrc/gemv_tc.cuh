@@ -278,12 +278,7 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_bd_kernel(Params p, int xbf16
 template <int FMT, int SK>
 static int32_t launch_t(const Params &p, bool xbf16, cudaStream_t stream) {
   const size_t smem = (size_t)p.m * p.cols * 2 + CHUNK * 2 + WARPS * 2 * ROWS * sizeof(float);
-  static bool attr = false;
-  if (!attr) {
-    B200_CUDA_TRY(
-        cudaFuncSetAttribute(gemv_bd_kernel<FMT, SK>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    attr = true;
-  }
+  B200_CUDA_TRY((ensure_dynamic_smem<gemv_bd_kernel<FMT, SK>>(200 * 1024)));
   const unsigned grid = (unsigned)((p.rows + ROWS - 1) / ROWS);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

@@ -466,13 +466,8 @@ static int32_t workspace_for(cudaStream_t stream, Workspace *&out) {
 template <int FMT, int NT, int SK, bool XBF16>
 static int32_t launch_t(const LinearArgs &a, int splits, float *ws, unsigned int *tickets, cudaStream_t stream) {
   constexpr int ESZ = tile_esz<SK>();
-  static bool attr = false;
   const size_t smem = smem_bytes<NT>(ESZ);
-  if (!attr) {
-    B200_CUDA_TRY(cudaFuncSetAttribute(skinny_kernel<FMT, NT, SK, XBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem));
-    attr = true;
-  }
+  B200_CUDA_TRY((ensure_dynamic_smem<skinny_kernel<FMT, NT, SK, XBF16>>((int)smem)));
   CUtensorMap tmw, tmx, tms;
   const uint64_t row_bytes = (uint64_t)a.cols / 2;
   if (int32_t rc = make_tma_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, row_bytes, (uint64_t)a.rows, row_bytes, 128,
@@ -572,12 +567,8 @@ bool skinny_supported(const LinearArgs &a) {
 
 int32_t launch_skinny(const LinearArgs &a, cudaStream_t stream) {
   using namespace skinny;
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    B200_CUDA_TRY(cudaGetDevice(&dev));
-    B200_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  }
+  int sms = 0;
+  B200_CUDA_TRY(device_sms(&sms));
   int splits = choose_splits(a, sms * (a.m <= 16 ? 2 : 1));
   float *ws = nullptr;
   unsigned int *tickets = nullptr;
@@ -642,12 +633,8 @@ static int32_t noalloc_scratch(unsigned char *&base) {
 
 int32_t launch_skinny_noalloc(const LinearArgs &a, cudaStream_t stream) {
   using namespace skinny;
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    B200_CUDA_TRY(cudaGetDevice(&dev));
-    B200_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  }
+  int sms = 0;
+  B200_CUDA_TRY(device_sms(&sms));
   const int splits = choose_splits(a, sms * (a.m <= 16 ? 2 : 1));  // as b200_packed_linear
   float *ws = nullptr;
   unsigned int *tickets = nullptr;
