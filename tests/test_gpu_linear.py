@@ -104,6 +104,17 @@ def test_odd_shapes(rows, cols, m, fmt):
     _run(spec, None, m, "float16", "float32", "auto")
 
 
+@pytest.mark.parametrize("rows", [4736, 4768])
+@pytest.mark.parametrize("fmt,kind,scale", [("fp4_e2m1", "e8m0", "e8m0"), ("fp6_e3m2", "f16u", None),
+                                            ("int4", "f16u", None)])
+@pytest.mark.parametrize("m", [1, 2])
+def test_decode_gemv_consumer_counts(rows, fmt, kind, scale, m):
+    """148 and 149 row blocks of 32 rows: on a 148-SM B200 the streamed GEMV runs 16 consumer
+    warps per CTA in the first case (one row block per CTA) and 8 in the second."""
+    spec = _spec(fmt, rows, 1024, 32, kind, 5)
+    _run(spec, scale, m, "bfloat16", "bfloat16", "gemv")
+
+
 @pytest.mark.parametrize("ydt", ["float16", "bfloat16", "float32"])
 def test_output_dtypes(ydt):
     spec = ref.make_packed(np.random.default_rng(11), "fp4_e2m1", 512, 1024, 32, "e8m0")

@@ -8,13 +8,14 @@
 //
 // Structure (Blackwell-native streaming):
 //   * persistent CTAs (as many per SM as fit); CTA c owns a contiguous range of 32-row blocks;
-//   * warp 8, lane 0 is a TMA producer: for each row block it streams 32 rows x 512 payloads
-//     per stage (256 B/row for 4-bit, 384 B/row for 6-bit) plus the stage's per-32 block
-//     scales into a shared-memory ring (~80 KB in flight per CTA, no registers), signalled by
-//     mbarrier transaction counts; it starts before the programmatic-dependency wait because
-//     weights and scales are parameters, not outputs of the previous kernel;
-//   * warps 0-7 consume: four warps per stage, one 128-payload chunk each. A lane reads its
-//     32-payload blocks of rows g, g+8, g+16, g+24 from shared memory, decodes them to exact
+//   * the last warp's lane 0 is a TMA producer: for each row block it streams 32 rows x 512
+//     payloads per stage (256 B/row for 4-bit, 384 B/row for 6-bit) plus the stage's per-32
+//     block scales into a shared-memory ring (~80 KB in flight per CTA, no registers),
+//     signalled by mbarrier transaction counts; it starts before the programmatic-dependency
+//     wait because weights and scales are parameters, not outputs of the previous kernel;
+//   * warps 0-7 (0-15 when no CTA takes more than one row block) consume: four warps per
+//     stage, one 128-payload chunk each. A lane reads its 32-payload blocks of rows g, g+8,
+//     g+16, g+24 from shared memory, decodes them to exact
 //     fp16 (gemv_tc.cuh) and feeds two independent mma.sync m16n8k16 chains with the
 //     block-diagonal activation operand, so every accumulator column is one block's partial
 //     sum, scaled in fp32 (exact for every scale dtype);
@@ -37,8 +38,13 @@ int32_t gemv_device_error(unsigned int *v, bool clear) {
 namespace gemvs {
 using namespace gemv;
 
-constexpr int CONSUMERS = 8, THREADS = (CONSUMERS + 1) * 32;
-constexpr int CPS = 4;               // 128-payload chunks per stage (one per consumer of a parity)
+// NC consumer warps (8 or 16) plus one TMA producer warp; the consumers form NC / CPS groups and
+// group q takes the stages st with st % (NC / CPS) == q.
+template <int NC>
+__host__ __device__ constexpr int threads() {
+  return (NC + 1) * 32;
+}
+constexpr int CPS = 4;               // 128-payload chunks per stage (one per consumer warp of a group)
 constexpr int KSTAGE = CPS * CHUNK;  // payloads per row per stage (512)
 constexpr int RB = 32;               // rows per block: two m16 row groups per lane
 
@@ -158,13 +164,13 @@ struct StreamParams {
 };
 
 // stage x[m][K] as fp16 in decode pair order (consumer threads only)
-template <int FMT>
+template <int FMT, int NC>
 __device__ __forceinline__ bool stage_x_consumers(const Params &p, __half *xs, int K, int tid, bool xbf16,
                                                   float prescale) {
   bool ok = true;
   for (int mm = 0; mm < (int)p.m; ++mm) {
     const uint16_t *src = (const uint16_t *)p.x + (int64_t)mm * p.ldx;
-    for (int k8 = tid; k8 < (K >> 3); k8 += CONSUMERS * 32) {
+    for (int k8 = tid; k8 < (K >> 3); k8 += NC * 32) {
       const uint4 u = __ldg(reinterpret_cast<const uint4 *>(src) + k8);
       const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
       uint32_t h[8];
@@ -190,12 +196,13 @@ __device__ __forceinline__ bool stage_x_consumers(const Params &p, __half *xs, i
   return ok;
 }
 
+template <int NC>
 __device__ __forceinline__ void consumer_sync() {
-  asm volatile("bar.sync 1, %0;" ::"r"(CONSUMERS * 32) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
 }
 
-template <int FMT, int SK>
-__global__ void __launch_bounds__(THREADS, 1)
+template <int FMT, int SK, int NC>
+__global__ void __launch_bounds__(threads<NC>(), 1)
     gemv_stream_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tms,
                        StreamParams sp) {
   constexpr int BITS = Fmt<FMT>::bits;
@@ -213,8 +220,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile uint32_t *abort_flag = reinterpret_cast<uint32_t *>(empty + STAGES);
   volatile uint32_t *ovf_flag = abort_flag + 1;
   // 16-byte aligned: zslot and xs below take 128-bit stores
-  float *red = reinterpret_cast<float *>(((uintptr_t)(empty + STAGES + 1) + 15) & ~(uintptr_t)15);  // [2][8][2][RB]
-  __half *zslot = reinterpret_cast<__half *>(red + 2 * CONSUMERS * 2 * RB);  // CHUNK zeros
+  float *red = reinterpret_cast<float *>(((uintptr_t)(empty + STAGES + 1) + 15) & ~(uintptr_t)15);  // [2][NC][2][RB]
+  __half *zslot = reinterpret_cast<__half *>(red + 2 * NC * 2 * RB);  // CHUNK zeros
   __half *xs = zslot + CHUNK;                                              // [m][K]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -233,7 +240,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  if (warp == CONSUMERS) {
+  if (warp == NC) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       prefetch_tmap(&tmw);
@@ -270,25 +277,25 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int g = lane >> 2, t = lane & 3;
   const int cm = t >> 1, cblk = 2 * (t & 1);
   const int sub = warp % CPS;     // chunk within a stage
-  const int parity = warp / CPS;  // this warp consumes stages st with st % 2 == parity
+  const int group = warp / CPS;  // this warp consumes stages st with st % (NC / CPS) == group
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (tid < CHUNK / 8) reinterpret_cast<uint4 *>(zslot)[tid] = make_uint4(0u, 0u, 0u, 0u);
   float prescale = 1.f;
-  if (!stage_x_consumers<FMT>(p, xs, K, tid, sp.xbf16 != 0, 1.f)) *ovf_flag = 1;
-  consumer_sync();
+  if (!stage_x_consumers<FMT, NC>(p, xs, K, tid, sp.xbf16 != 0, 1.f)) *ovf_flag = 1;
+  consumer_sync<NC>();
   if (*ovf_flag) {  // rare: bf16 beyond fp16 range -> power-of-two prescale so max|x| < 2^15
     float amax = 0.f;
     for (int mm = 0; mm < (int)p.m; ++mm)
-      for (int k = tid; k < K; k += CONSUMERS * 32)
+      for (int k = tid; k < K; k += NC * 32)
         amax = fmaxf(amax, fabsf(__bfloat162float(((const __nv_bfloat16 *)p.x)[(int64_t)mm * p.ldx + k])));
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     if (lane == 0) red[warp] = amax;
-    consumer_sync();
-    for (int wv = 0; wv < CONSUMERS; ++wv) amax = fmaxf(amax, red[wv]);
+    consumer_sync<NC>();
+    for (int wv = 0; wv < NC; ++wv) amax = fmaxf(amax, red[wv]);
     const int ex = ((__float_as_int(amax) >> 23) & 0xFF) - 127;
     prescale = __int_as_float((127 - (ex - 14)) << 23);
-    stage_x_consumers<FMT>(p, xs, K, tid, true, prescale);
-    consumer_sync();
+    stage_x_consumers<FMT, NC>(p, xs, K, tid, true, prescale);
+    consumer_sync<NC>();
   }
 
   const int bm = g >> 2;
@@ -300,7 +307,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   for (int64_t rbk = rb_begin; rbk < rb_end; ++rbk) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, g+16, g+24 for m = cm
     for (int st = 0; st < sp.nst; ++st, (++slot == STAGES ? (slot = 0, round ^= 1u) : 0u)) {
-      if ((st & 1) != parity) continue;
+      if ((unsigned)st % (NC / CPS) != (unsigned)group) continue;
       const bool got = mbar_wait(&full[slot], round, abort_flag);
       const uint8_t *base = ring + slot * SLOT;
       Chunk4<BITS> r;
@@ -346,22 +353,22 @@ __global__ void __launch_bounds__(THREADS, 1)
         compute_chunk4<FMT, SK>(r, owner ? xrow + (int64_t)chunk * CHUNK : zslot, acc);
       }
     }
-    // ---- reduce this row block over the 8 consumer warps and store ----
+    // ---- reduce this row block over the NC consumer warps and store ----
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 1);
-    float *rb = red + buf * (CONSUMERS * 2 * RB);
+    float *rb = red + buf * (NC * 2 * RB);
     if ((t & 1) == 0) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) rb[(warp * 2 + cm) * RB + g + 8 * i] = acc[i];
     }
-    consumer_sync();
+    consumer_sync<NC>();
     if (tid < 2 * RB) {
       const int mm = tid / RB, rr = tid % RB;
       const int64_t n = rbk * RB + rr;
       if (mm < p.m && n < p.rows && !*abort_flag) {
         float s = 0.f;
 #pragma unroll
-        for (int wv = 0; wv < CONSUMERS; ++wv) s += rb[(wv * 2 + mm) * RB + rr];
+        for (int wv = 0; wv < NC; ++wv) s += rb[(wv * 2 + mm) * RB + rr];
         s *= place_factor<FMT>() / prescale;
         if constexpr (SK == SK_ROW) s *= load_as_f32(p.scales, n * p.nblk, p.sdt);
         store_f32(p.y, mm * p.ldy_m + n * p.ldy_n, p.ydt, s);
@@ -372,22 +379,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-template <int BITS, int SESZ>
+template <int BITS, int SESZ, int NC>
 static size_t smem_bytes(int64_t m, int64_t cols) {
   return 128 + (size_t)ring_stages<BITS>() * slot_bytes(BITS, SESZ) + 2 * ring_stages<BITS>() * 8 + 8 + 16 +
-         2 * CONSUMERS * 2 * RB * 4 + CHUNK * 2 + (size_t)m * cols * 2;
+         2 * NC * 2 * RB * 4 + CHUNK * 2 + (size_t)m * cols * 2;
 }
 
-template <int FMT, int SK>
+template <int FMT, int SK, int NC>
 static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
   constexpr int BITS = Fmt<FMT>::bits;
   constexpr int SESZ = scale_esz<SK>();
-  const size_t smem = smem_bytes<BITS, SESZ>(a.m, a.cols);
+  const size_t smem = smem_bytes<BITS, SESZ, NC>(a.m, a.cols);
   int sms = 0;
   B200_CUDA_TRY(device_sms(&sms));
-  B200_CUDA_TRY((ensure_dynamic_smem<gemv_stream_kernel<FMT, SK>>(200 * 1024)));
+  B200_CUDA_TRY((ensure_dynamic_smem<gemv_stream_kernel<FMT, SK, NC>>(200 * 1024)));
   int per_sm = 0;
-  B200_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stream_kernel<FMT, SK>, THREADS, smem));
+  B200_CUDA_TRY(
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stream_kernel<FMT, SK, NC>, threads<NC>(), smem));
   if (per_sm < 1) return b200_set_error(B200_ERR_UNSUPPORTED, "streamed GEMV: no CTA fits (%zu B smem)", smem);
   CUtensorMap tmw, tms;
   const uint64_t row_bytes = (uint64_t)a.cols * BITS / 8;
@@ -419,7 +427,7 @@ static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
   const int64_t grid = sp.nrb < slots ? sp.nrb : slots;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3(THREADS);
+  cfg.blockDim = dim3(threads<NC>());
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attrs[1];
@@ -427,19 +435,33 @@ static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
   attrs[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = (a.flags & B200_FLAG_PDL) ? 1 : 0;
-  B200_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stream_kernel<FMT, SK>, tmw, tms, sp));
+  B200_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stream_kernel<FMT, SK, NC>, tmw, tms, sp));
   return B200_OK;
+}
+
+// 16 consumer warps when no CTA takes more than one row block: a lone row block is latency
+// bound and twice the warps halve its stage rounds (FP4, M=1: 1280 x 8192 8.7 -> 6.4 us,
+// 4096 x 4096 5.8 -> 4.3 us). CTAs that stream several row blocks keep 8 (16 measured slower:
+// 8192 x 8192 10.5 -> 11.4 us, 28672 x 8192 28.9 -> 34 us).
+template <int FMT, int SK>
+static int32_t launch_nc(const LinearArgs &a, cudaStream_t stream) {
+  int sms = 0;
+  B200_CUDA_TRY(device_sms(&sms));
+  const int64_t nrb = (a.rows + RB - 1) / RB;
+  if (nrb <= sms && smem_bytes<Fmt<FMT>::bits, scale_esz<SK>(), 16>(a.m, a.cols) <= 200 * 1024)
+    return launch_t<FMT, SK, 16>(a, stream);
+  return launch_t<FMT, SK, 8>(a, stream);
 }
 
 template <int FMT>
 static int32_t dispatch_sk(const LinearArgs &a, int sk, cudaStream_t stream) {
   switch (sk) {
-    case SK_NONE: return launch_t<FMT, SK_NONE>(a, stream);
-    case SK_ROW: return launch_t<FMT, SK_ROW>(a, stream);
-    case SK_E8M0: return launch_t<FMT, SK_E8M0>(a, stream);
-    case SK_F16: return launch_t<FMT, SK_F16>(a, stream);
-    case SK_BF16: return launch_t<FMT, SK_BF16>(a, stream);
-    case SK_F32: return launch_t<FMT, SK_F32>(a, stream);
+    case SK_NONE: return launch_nc<FMT, SK_NONE>(a, stream);
+    case SK_ROW: return launch_nc<FMT, SK_ROW>(a, stream);
+    case SK_E8M0: return launch_nc<FMT, SK_E8M0>(a, stream);
+    case SK_F16: return launch_nc<FMT, SK_F16>(a, stream);
+    case SK_BF16: return launch_nc<FMT, SK_BF16>(a, stream);
+    case SK_F32: return launch_nc<FMT, SK_F32>(a, stream);
   }
   return b200_set_error(B200_ERR_UNSUPPORTED, "streamed GEMV: scale layout");
 }
@@ -461,7 +483,7 @@ bool gemv_stream_supported(const LinearArgs &a) {
   }
   const int bits = fmt_bits(a.fmt);
   if ((uintptr_t)a.w % 16 != 0 || ((uint64_t)a.cols * bits / 8) % 16 != 0) return false;
-  const size_t smem = bits == 4 ? smem_bytes<4, 4>(a.m, a.cols) : smem_bytes<6, 4>(a.m, a.cols);
+  const size_t smem = bits == 4 ? smem_bytes<4, 4, 8>(a.m, a.cols) : smem_bytes<6, 4, 8>(a.m, a.cols);
   return smem <= 200 * 1024;
 }
 
