@@ -163,34 +163,47 @@ struct StreamParams {
   int xbf16;
 };
 
-// stage x[m][K] as fp16 in decode pair order (consumer threads only)
+// stage x[m][K] as fp16 in decode pair order (consumer threads only). Each thread issues up to
+// XB 16-byte loads before converting any, so the staging costs about one memory round trip.
 template <int FMT, int NC>
 __device__ __forceinline__ bool stage_x_consumers(const Params &p, __half *xs, int K, int tid, bool xbf16,
                                                   float prescale) {
+  constexpr int XB = 4;
   bool ok = true;
+  const int n8 = K >> 3;
   for (int mm = 0; mm < (int)p.m; ++mm) {
-    const uint16_t *src = (const uint16_t *)p.x + (int64_t)mm * p.ldx;
-    for (int k8 = tid; k8 < (K >> 3); k8 += NC * 32) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4 *>(src) + k8);
-      const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
-      uint32_t h[8];
+    const uint4 *src = reinterpret_cast<const uint4 *>((const uint16_t *)p.x + (int64_t)mm * p.ldx);
+    for (int k0 = tid; k0 < n8; k0 += XB * NC * 32) {
+      uint4 u[XB];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (xbf16) {
-          const __half lo = __float2half_rn(__uint_as_float(wv[i] << 16) * prescale);
-          const __half hi = __float2half_rn(__uint_as_float(wv[i] & 0xFFFF0000u) * prescale);
-          ok = ok && !(__hisinf(lo) | __hisinf(hi));
-          h[2 * i] = __half_as_ushort(lo), h[2 * i + 1] = __half_as_ushort(hi);
-        } else {
-          h[2 * i] = wv[i] & 0xFFFFu, h[2 * i + 1] = wv[i] >> 16;
-        }
+      for (int j = 0; j < XB; ++j) {
+        const int k8 = k0 + j * NC * 32;
+        u[j] = k8 < n8 ? __ldg(src + k8) : make_uint4(0u, 0u, 0u, 0u);
       }
-      uint4 o;
-      if constexpr (pairs_04<FMT>())
-        o = make_uint4(h[0] | (h[4] << 16), h[1] | (h[5] << 16), h[2] | (h[6] << 16), h[3] | (h[7] << 16));
-      else
-        o = make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
-      *reinterpret_cast<uint4 *>(xs + (int64_t)mm * K + 8 * k8) = o;
+#pragma unroll
+      for (int j = 0; j < XB; ++j) {
+        const int k8 = k0 + j * NC * 32;
+        if (k8 >= n8) break;
+        const uint32_t wv[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
+        uint32_t h[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (xbf16) {
+            const __half lo = __float2half_rn(__uint_as_float(wv[i] << 16) * prescale);
+            const __half hi = __float2half_rn(__uint_as_float(wv[i] & 0xFFFF0000u) * prescale);
+            ok = ok && !(__hisinf(lo) | __hisinf(hi));
+            h[2 * i] = __half_as_ushort(lo), h[2 * i + 1] = __half_as_ushort(hi);
+          } else {
+            h[2 * i] = wv[i] & 0xFFFFu, h[2 * i + 1] = wv[i] >> 16;
+          }
+        }
+        uint4 o;
+        if constexpr (pairs_04<FMT>())
+          o = make_uint4(h[0] | (h[4] << 16), h[1] | (h[5] << 16), h[2] | (h[6] << 16), h[3] | (h[7] << 16));
+        else
+          o = make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
+        *reinterpret_cast<uint4 *>(xs + (int64_t)mm * K + 8 * k8) = o;
+      }
     }
   }
   return ok;
