@@ -11,7 +11,9 @@
 //   * warp 8, lane 0 streams per stage (512 K) the rows' packed codes (two 128-byte-swizzled
 //     TMA boxes), x[0:8*NT, stage] (eight 128-byte-swizzled boxes, rows past M zero-filled)
 //     and, for per-32 scales, the stage's scale tile into a shared-memory ring;
-//   * warps 0-7 consume: warp w owns rows 16w..16w+15. ldmatrix hands lane (g, t) payloads
+//   * warps 0-7 consume: warp w owns rows 16w..16w+15 (the 32-token tile runs warps 0-15, warp
+//     w and w+8 sharing rows 16(w%8).. and taking the first / second half of each stage's
+//     blocks, then adding their sums through shared memory). ldmatrix hands lane (g, t) payloads
 //     8t..8t+7 of one 32-payload block for rows g and g+8; the sm_100a conversions decode them
 //     to exact fp16; two mma.sync m16n8k16 per block and token tile give the block's partial
 //     sum for 8 tokens, scaled in fp32 by the block's scale (exact for every scale dtype).
@@ -40,8 +42,20 @@ int32_t skinny_device_error(unsigned int *v, bool clear) {
 namespace skinny {
 using namespace gemv;
 
-constexpr int CONSUMERS = 8, THREADS = (CONSUMERS + 1) * 32;
-constexpr int RB = 128;                 // weight rows per CTA (16 per consumer warp)
+constexpr int RB = 128;                 // weight rows per CTA (16 per consumer row group)
+// Consumer warps: eight row groups of 16 rows. The 32-token tile (one CTA per SM) runs two warps
+// per row group, each taking half of every stage's 32-payload blocks, so that the SM keeps 16
+// consumer warps (M=32, FP4 E8M0: 52 -> 47 us); the smaller tiles run one warp per row group and
+// two CTAs per SM. Wide group scales and per-32 fp32 scales keep one warp per row group: their
+// scale registers would not fit the 96 registers that 17 warps leave per thread.
+template <int NT, int SK>
+__host__ __device__ constexpr int consumers() {
+  return NT == 4 && SK != gemv::SK_GROUP && SK != gemv::SK_F32 ? 16 : 8;
+}
+template <int NT, int SK>
+__host__ __device__ constexpr int threads() {
+  return (consumers<NT, SK>() + 1) * 32;
+}
 constexpr int KST = 512;                // payloads per row per stage
 constexpr int W_BYTES = RB * KST / 2;   // 4-bit codes: 32 KB per stage
 template <int NT>
@@ -113,13 +127,16 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t &d0, uint32_
                : "r"(addr));
 }
 
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CONSUMERS * 32) : "memory"); }
+template <int NC>
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(NC * 32) : "memory");
+}
 
 // bf16 x chunk of the slot -> fp16 in place with a per-token power-of-two prescale; writes
 // the inverse factors to inv[8*NT]. Tokens are the box rows (8*NT per box, 8 boxes).
-template <int NT>
+template <int NT, int NC>
 __device__ __forceinline__ void convert_x(uint8_t *xs, float *inv, int tid) {
-  constexpr int TOK = 8 * NT, TPT = CONSUMERS * 32 / TOK;  // threads per token
+  constexpr int TOK = 8 * NT, TPT = NC * 32 / TOK;  // threads per token
   const int tok = tid / TPT, part = tid % TPT;
   // each token row holds 8 boxes x 8 chunks of 16 bytes = 64 chunks (positions are swizzled,
   // which does not matter for an elementwise conversion)
@@ -153,7 +170,7 @@ __device__ __forceinline__ void convert_x(uint8_t *xs, float *inv, int tid) {
 }
 
 template <int FMT, int NT, int SK, bool XBF16>
-__global__ void __launch_bounds__(THREADS, ctas_per_sm<NT>())
+__global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
     skinny_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
                   const __grid_constant__ CUtensorMap tms, SkParams p) {
   constexpr int ESZ = tile_esz<SK>();
@@ -161,6 +178,9 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm<NT>())
   constexpr int SLOT = slot_bytes<NT>(ESZ);
   constexpr int STAGES = stages<NT>(ESZ);
   constexpr int TOK = 8 * NT;
+  constexpr int NC = consumers<NT, SK>();
+  constexpr int KH = NC / 8;         // warps per row group; each takes 1/KH of a stage's blocks
+  constexpr int NB = KST / 32 / KH;  // 32-payload blocks per warp and stage
   constexpr uint32_t TX = W_BYTES + x_bytes<NT>() + (TILE_SCALES ? s_bytes(ESZ) : 0);
   extern __shared__ uint8_t smem_raw[];
   uint8_t *ring = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -177,7 +197,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm<NT>())
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], CONSUMERS);
+      mbar_init(&empty[s], NC);
     }
     *abort_flag = 0;
     *last_flag = 0;
@@ -185,7 +205,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm<NT>())
   }
   __syncthreads();
 
-  if (warp == CONSUMERS) {
+  if (warp == NC) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       prefetch_tmap(&tmw);
@@ -221,7 +241,8 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm<NT>())
 
   // ---------------- consumers ----------------
   const int g = lane >> 2, t = lane & 3;
-  const int r0 = warp * 16;  // this warp's rows r0 + g, r0 + g + 8 (within the CTA's 128)
+  const int kh = KH == 1 ? 0 : warp / 8;  // which part of each stage's blocks this warp takes
+  const int r0 = (KH == 1 ? warp : warp % 8) * 16;  // rows r0 + g, r0 + g + 8 (within the CTA's 128)
   const int64_t nlo = (int64_t)rblk * RB + r0 + g, nhi = nlo + 8;
   float acc[NT][4];
 #pragma unroll
@@ -238,15 +259,16 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm<NT>())
   for (int st = st0; st < st1; ++st) {
     // SK_GROUP: the scales of the groups that end in this stage, indexed by their last block
     // (prefetched before the stage wait; compile-time indices keep them in registers)
-    float sgl[KST / 32], sgh[KST / 32];
+    float sgl[NB], sgh[NB];  // indexed by the warp's local block j (stage block kh * NB + j)
     if constexpr (SK == SK_GROUP) {
 #pragma unroll
-      for (int bb = 0; bb < KST / 32; ++bb) {
-        sgl[bb] = sgh[bb] = 0.f;
+      for (int j = 0; j < NB; ++j) {
+        const int bb = kh * NB + j;
+        sgl[j] = sgh[j] = 0.f;
         if (((32 * (bb + 1)) & (p.block - 1)) == 0) {
           const int64_t gi = ((int64_t)st * KST + 32 * bb) >> p.block_log2;
-          if (nlo < p.rows) sgl[bb] = load_as_f32(p.scales, nlo * p.nblk + gi, p.sdt);
-          if (nhi < p.rows) sgh[bb] = load_as_f32(p.scales, nhi * p.nblk + gi, p.sdt);
+          if (nlo < p.rows) sgl[j] = load_as_f32(p.scales, nlo * p.nblk + gi, p.sdt);
+          if (nhi < p.rows) sgh[j] = load_as_f32(p.scales, nhi * p.nblk + gi, p.sdt);
         }
       }
     }
@@ -255,8 +277,8 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm<NT>())
     uint8_t *xs = base + W_BYTES;
     float *sinv = inv + slot * TOK;
     if constexpr (XBF16) {
-      if (got) convert_x<NT>(xs, sinv, tid);
-      consumer_sync();
+      if (got) convert_x<NT, NC>(xs, sinv, tid);
+      consumer_sync<NC>();
     }
     float sacc[NT][4];
 #pragma unroll
@@ -265,26 +287,35 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm<NT>())
       const uint8_t *srow_lo = base + W_BYTES + x_bytes<NT>() + (r0 + g) * (KST / 32) * ESZ;
       const uint8_t *srow_hi = srow_lo + 8 * (KST / 32) * ESZ;
       const uint32_t wbase = smem_u32(base);
-      uint4 e8lo = make_uint4(0u, 0u, 0u, 0u), e8hi = e8lo;  // the stage's 16 E8M0 scales of rows g / g+8
+      // the E8M0 scales of this warp's NB blocks, rows g / g+8 (word i holds local blocks 4i..4i+3)
+      uint32_t e8l[SK == SK_E8M0 ? NB / 4 : 1] = {}, e8h[SK == SK_E8M0 ? NB / 4 : 1] = {};
       bool e8fast = false;
       if constexpr (SK == SK_E8M0) {
-        e8lo = *reinterpret_cast<const uint4 *>(srow_lo);
-        e8hi = *reinterpret_cast<const uint4 *>(srow_hi);
+        if constexpr (NB == 16) {
+          const uint4 ul = *reinterpret_cast<const uint4 *>(srow_lo), uh = *reinterpret_cast<const uint4 *>(srow_hi);
+          e8l[0] = ul.x, e8l[1] = ul.y, e8l[2] = ul.z, e8l[3] = ul.w;
+          e8h[0] = uh.x, e8h[1] = uh.y, e8h[2] = uh.z, e8h[3] = uh.w;
+        } else {
+          const uint2 ul = *reinterpret_cast<const uint2 *>(srow_lo + kh * NB);
+          const uint2 uh = *reinterpret_cast<const uint2 *>(srow_hi + kh * NB);
+          e8l[0] = ul.x, e8l[1] = ul.y, e8h[0] = uh.x, e8h[1] = uh.y;
+        }
         // a normal fp16 2^e with e in [-14, 12] multiplies every decoded 4-bit payload exactly
         // (at most two significant bits, 0.5 <= |value| <= 8: products stay within fp16, down to
         // its subnormal quantum 2^-24): E8M0 bytes 113..139
-        const uint32_t wv[8] = {e8lo.x, e8lo.y, e8lo.z, e8lo.w, e8hi.x, e8hi.y, e8hi.z, e8hi.w};
         uint32_t inr = 0xFFFFFFFFu;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) inr &= __vcmpgeu4(wv[i], 0x71717171u) & __vcmpleu4(wv[i], 0x8B8B8B8Bu);
+        for (int i = 0; i < NB / 4; ++i)
+          inr &= __vcmpgeu4(e8l[i], 0x71717171u) & __vcmpleu4(e8l[i], 0x8B8B8B8Bu) & __vcmpgeu4(e8h[i], 0x71717171u) &
+                 __vcmpleu4(e8h[i], 0x8B8B8B8Bu);
         e8fast = __all_sync(0xffffffffu, inr == 0xFFFFFFFFu);
       }
       float gd[NT][4];  // running partial of the current scale group (SK_GROUP)
 #pragma unroll
       for (int j = 0; j < NT; ++j) gd[j][0] = gd[j][1] = gd[j][2] = gd[j][3] = 0.f;
 #pragma unroll
-      for (int bp = 0; bp < KST / 64; ++bp) {  // pairs of 32-payload blocks
-        const int b = 2 * bp;
+      for (int jp = 0; jp < NB / 2; ++jp) {  // pairs of this warp's 32-payload blocks
+        const int b = kh * NB + 2 * jp;
         const int box = b >> 3, chunk = (b & 7) + lchunk;
         uint32_t wl0, wh0, wl1, wh1;  // rows g / g+8 of blocks b / b+1
         ldmatrix_x4(wbase + box * (RB * 128) + lrow * 128 + (((chunk) ^ (lrow & 7)) << 4), wl0, wh0, wl1, wh1);
@@ -298,9 +329,8 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm<NT>())
           const int xbox = bb >> 1;
           float sl = 1.f, sh = 1.f;
           if constexpr (SK == SK_E8M0) {
-            const uint32_t wlo = bb < 4 ? e8lo.x : bb < 8 ? e8lo.y : bb < 12 ? e8lo.z : e8lo.w;
-            const uint32_t whi = bb < 4 ? e8hi.x : bb < 8 ? e8hi.y : bb < 12 ? e8hi.z : e8hi.w;
-            const uint32_t bl = (wlo >> (8 * (bb & 3))) & 0xFFu, bh = (whi >> (8 * (bb & 3))) & 0xFFu;
+            const int jb = 2 * jp + h;  // local block: compile-time word and byte
+            const uint32_t bl = (e8l[jb >> 2] >> (8 * (jb & 3))) & 0xFFu, bh = (e8h[jb >> 2] >> (8 * (jb & 3))) & 0xFFu;
             if (e8fast) {  // fp16 2^(b-127) = bits (b - 112) << 10, exact in range; both halves
               const uint32_t hl = (bl - 112u) << 10, hh = (bh - 112u) << 10;
               const __half2 s2l = __halves2half2(__ushort_as_half((unsigned short)hl), __ushort_as_half((unsigned short)hl));
@@ -345,7 +375,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm<NT>())
           }
           if constexpr (SK == SK_GROUP) {
             if (((32 * (bb + 1)) & (p.block - 1)) == 0) {  // the group ends with this block
-              const float gl = sgl[bb], gh = sgh[bb];
+              const float gl = sgl[2 * jp + h], gh = sgh[2 * jp + h];
 #pragma unroll
               for (int j = 0; j < NT; ++j) {
                 sacc[j][0] = fmaf(gd[j][0], gl, sacc[j][0]);
@@ -374,7 +404,27 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm<NT>())
     if (++slot == STAGES) slot = 0, ph ^= 1u;
   }
 
-  // ---------------- epilogue ----------------
+  if constexpr (KH == 2) {
+    // the second warp of each row group hands its sums to the first through the ring, which is
+    // idle now: every stage has been consumed, so no copy is in flight
+    float *pair = reinterpret_cast<float *>(ring);  // [8 row groups][NT * 4][32 lanes]
+    consumer_sync<NC>();
+    if (kh == 1) {
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pair[((warp - 8) * NT * 4 + 4 * j + i) * 32 + lane] = acc[j][i];
+    }
+    consumer_sync<NC>();
+    if (kh == 0) {
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[j][i] += pair[(warp * NT * 4 + 4 * j + i) * 32 + lane];
+    }
+  }
+
+  // ---------------- epilogue (first warp of each row group) ----------------
   const bool ok = !*abort_flag;
   float rs_lo = 1.f, rs_hi = 1.f;
   if constexpr (SK == SK_ROW) {
@@ -382,7 +432,7 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm<NT>())
     if (nhi < p.rows) rs_hi = load_as_f32(p.scales, nhi * p.nblk, p.sdt);
   }
   if (p.splits == 1) {
-    if (!ok) return;
+    if (!ok || kh != 0) return;
 #pragma unroll
     for (int j = 0; j < NT; ++j)
 #pragma unroll
@@ -398,19 +448,19 @@ __global__ void __launch_bounds__(THREADS, ctas_per_sm<NT>())
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int64_t m = 8 * j + 2 * t + (i & 1), n = i < 2 ? nlo : nhi;
-      if (m < p.m && n < p.rows) p.ws[((int64_t)split * p.m + m) * p.rows + n] = acc[j][i];
+      if (kh == 0 && m < p.m && n < p.rows) p.ws[((int64_t)split * p.m + m) * p.rows + n] = acc[j][i];
     }
   __threadfence();
-  consumer_sync();
+  consumer_sync<NC>();
   if (tid == 0) {
     const unsigned int ticket = atomicAdd(&p.tickets[rblk], 1u);
     *last_flag = ticket == (unsigned int)(p.splits - 1);
   }
-  consumer_sync();
+  consumer_sync<NC>();
   if (!*last_flag) return;
   __threadfence();
   const int64_t n0 = (int64_t)rblk * RB;
-  for (int e = tid; e < RB * (int)p.m; e += CONSUMERS * 32) {
+  for (int e = tid; e < RB * (int)p.m; e += NC * 32) {
     const int64_t m = e / RB, n = n0 + e % RB;
     if (n >= p.rows) continue;
     float s = 0.f;
@@ -499,7 +549,7 @@ static int32_t launch_t(const LinearArgs &a, int splits, float *ws, unsigned int
   p.ws = ws;
   p.tickets = tickets;
   const int64_t nrb = (a.rows + RB - 1) / RB;
-  skinny_kernel<FMT, NT, SK, XBF16><<<(unsigned)(nrb * splits), THREADS, smem, stream>>>(tmw, tmx, tms, p);
+  skinny_kernel<FMT, NT, SK, XBF16><<<(unsigned)(nrb * splits), threads<NT, SK>(), smem, stream>>>(tmw, tmx, tms, p);
   B200_LAUNCH_CHECK();
   return B200_OK;
 }
