@@ -442,7 +442,7 @@ def run_configs(args, device, world, rank):
     # c4 INT4 stack, one token through 32 layers on this GPU (no tensor parallelism)
     st = S.TPStack(S.C4, 0, 1, device=device, seed=5 + rank)
     total = S.C4.layer_weight_bytes() * S.C4.layers
-    for m4 in (1, 16):
+    for m4 in (1, 16, 64):
         h0 = torch.randn((m4, S.C4.hidden), device=device).to(S.C4.act)
         h = h0.clone()
 

@@ -188,12 +188,14 @@ def test_group_scales_decode_gemv(bs, scale, m, fmt):
 @pytest.mark.parametrize("bs", [32, 128])
 def test_gemm_rejects_inexact_group_scales(bs):
     """Non-power-of-two group scales cannot be folded exactly into a 16-bit tcgen05 operand
-    (weight x scale needs up to 15 significant bits); the GEMM path declines them and the
-    exact fp32 kernels take these shapes (config c4 at M=64)."""
+    (weight x scale needs up to 15 significant bits); the GEMM path declines them. The decode
+    kernel's 64-token tile takes them up to 64 tokens (config c4 at M=64), the fp32 SIMT kernel
+    beyond."""
     import tinygrad_dx12_b200 as tg  # noqa: F401
     from tinygrad_dx12_b200.linalg import linear_plan
 
     spec = _spec("int4", 512, 4096, bs, "f16u", 41)
     w = to_device(spec, DEV, "float16")
     assert linear_plan(w, torch.float16, 64, torch.float16, "gemm") is None
-    assert linear_plan(w, torch.float16, 64, torch.float16, "auto") == "simt"
+    assert linear_plan(w, torch.float16, 64, torch.float16, "auto") == "gemv"
+    assert linear_plan(w, torch.float16, 65, torch.float16, "auto") == "simt"

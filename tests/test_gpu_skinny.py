@@ -1,5 +1,5 @@
-"""Split-K decode GEMM for a few tokens (3 <= M <= 32, 4-bit formats) against the float32
-oracle: every 4-bit format x scale layout (none, per-row, per-32 E8M0 / fp16 / bf16 / fp32,
+"""Split-K decode GEMM for a few tokens (3 <= M <= 32, and 33..64 for the scale layouts the
+tcgen05 GEMM declines; 4-bit formats) against the float32 oracle: every 4-bit format x scale layout (none, per-row, per-32 E8M0 / fp16 / bf16 / fp32,
 group 64 / 128 / 512), fp16 and bf16 x, f16 / bf16 / f32 y, token counts on both sides of
 the 8-token tile edges, shapes with one and many K slices and a ragged last row block, and
 bf16 activations beyond the fp16 range or far below it (the per-token prescale).
@@ -101,3 +101,31 @@ def test_repeated_calls_reuse_workspace():
     ys = [_packed_linear(w, x, torch.float32, "gemv") for _ in range(20)]
     for y in ys[1:]:
         assert torch.equal(y, ys[0])
+
+
+WIDE_SCALES = [("f16u", 32, "float16"), ("f16u", 32, "bfloat16"), ("f16u", 32, "float32"), ("f16u", 128, "float16"),
+               ("f16u", 512, "bfloat16")]
+
+
+@pytest.mark.parametrize("m", [33, 48, 64])
+@pytest.mark.parametrize("fmt", ["int4", "fp4_e2m1"])
+@pytest.mark.parametrize("kind,bs,sdt", WIDE_SCALES)
+@pytest.mark.parametrize("xdt", ["float16", "bfloat16"])
+def test_64_token_tile(m, fmt, kind, bs, sdt, xdt):
+    """33..64 tokens with the scale layouts the tcgen05 GEMM declines (per-32 non-E8M0, wider
+    groups): the 64-token tile, several K slices, ragged rows."""
+    spec = _case(fmt, 1000, 2048, bs, kind)
+    _check(spec, sdt, m, xdt, xdt)
+
+
+def test_64_token_tile_auto_plan():
+    """The automatic plan takes the decode kernel for c4-like operands at 33..64 tokens and the
+    tcgen05 GEMM where it applies (E8M0 per-32 scales)."""
+    from tinygrad_dx12_b200.linalg import linear_plan
+
+    c4 = to_device(_case("int4", 512, 4096, 128, "f16u"), DEV, "float16")
+    c2 = to_device(_case("fp4_e2m1", 512, 4096, 32, "e8m0"), DEV, "e8m0")
+    for m in (33, 64):
+        assert linear_plan(c4, torch.float16, m, torch.float16, "auto") == "gemv"
+        assert linear_plan(c2, torch.bfloat16, m, torch.bfloat16, "auto") == "gemm"
+    assert linear_plan(c4, torch.float16, 65, torch.float16, "auto") == "simt"

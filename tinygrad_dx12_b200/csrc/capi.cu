@@ -140,6 +140,7 @@ static int32_t plan(const LinearArgs &a, bool kstride_ok, int32_t path) {
     case B200_PATH_AUTO:
       if (a.m <= 32 && tc) return B200_PATH_GEMV;
       if (a.m > 32 && gm) return B200_PATH_GEMM;
+      if (a.m <= 64 && skinny_supported(a)) return B200_PATH_GEMV;  // scales the GEMM declines
       if (simt) return B200_PATH_SIMT;
       return B200_ERR_UNSUPPORTED;
     case B200_PATH_GEMV: return tc ? B200_PATH_GEMV : B200_ERR_UNSUPPORTED;
@@ -341,7 +342,7 @@ int32_t b200_packed_linear_noalloc(const b200_packed_desc *w, const void *x, int
   if (x == nullptr || y == nullptr) return b200_set_error(B200_ERR_INVALID, "null x or y");
   LinearArgs a;
   fill_linear(w, x, x_dtype, m, x_stride_m, 1, y, y_dtype, y_stride_m, 1, a);
-  if (m < 3 || !skinny_supported(a))
+  if (m < 3 || m > 32 || !skinny_supported(a))
     return b200_set_error(B200_ERR_UNSUPPORTED,
                           "packed_linear_noalloc: no split-K decode GEMM for format=%d scale_dtype=%d block=%lld "
                           "K=%lld x_dtype=%d y_dtype=%d m=%lld",

@@ -51,7 +51,8 @@ bool gemv_stream_supported(const LinearArgs &a);
 int32_t launch_gemv_stream(const LinearArgs &a, cudaStream_t stream);
 int32_t gemv_device_error(unsigned int *v, bool clear);
 
-// split-K mma.sync decode GEMM for 3 <= M <= 32, 4-bit formats (skinny.cu)
+// split-K mma.sync decode GEMM for 3 <= M <= 32, 4-bit formats (skinny.cu); also 33 <= M <= 64
+// with per-32 fp16 / bf16 / fp32 or wider group scales
 bool skinny_supported(const LinearArgs &a);
 int32_t launch_skinny(const LinearArgs &a, cudaStream_t stream);
 int32_t skinny_device_error(unsigned int *v, bool clear);

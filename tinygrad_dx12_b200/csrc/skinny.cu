@@ -1,4 +1,5 @@
-// skinny.cu -- packed decode GEMM for a few tokens (3 <= M <= 32), 4-bit formats.
+// skinny.cu -- packed decode GEMM for a few tokens (3 <= M <= 32; up to 64 for the scale layouts
+// the tcgen05 GEMM declines), 4-bit formats.
 //
 //   y[m, n] = sum_k x[m, k] * dequant(W)[n, k]
 //
@@ -130,6 +131,13 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t &d0, uint32_
 template <int NC>
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(NC * 32) : "memory");
+}
+
+// compile-time choice between two same-typed arrays (no runtime indexing of registers)
+template <bool FIRST, typename T>
+__device__ __forceinline__ T &pick(T &a, T &b) {
+  if constexpr (FIRST) return a;
+  else return b;
 }
 
 // bf16 x chunk of the slot -> fp16 in place with a per-token power-of-two prescale; writes
@@ -280,9 +288,14 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
       if (got) convert_x<NT, NC>(xs, sinv, tid);
       consumer_sync<NC>();
     }
-    float sacc[NT][4];
+    // the stage's partial sums: a separate array with bf16 x (its per-token prescale is undone
+    // per stage), the running sums themselves with fp16 x (saves 4 * NT registers)
+    float sacc_bf[NT][4];  // unused (and eliminated) with fp16 x
+    float(&sacc)[NT][4] = pick<XBF16>(sacc_bf, acc);
+    if constexpr (XBF16) {
 #pragma unroll
-    for (int j = 0; j < NT; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+      for (int j = 0; j < NT; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+    }
     if (got) {
       const uint8_t *srow_lo = base + W_BYTES + x_bytes<NT>() + (r0 + g) * (KST / 32) * ESZ;
       const uint8_t *srow_hi = srow_lo + 8 * (KST / 32) * ESZ;
@@ -393,13 +406,15 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
     if constexpr (XBF16) fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
+    if constexpr (XBF16) {
 #pragma unroll
-    for (int j = 0; j < NT; ++j) {
-      const float f0 = XBF16 ? sinv[8 * j + 2 * t] : 1.f, f1 = XBF16 ? sinv[8 * j + 2 * t + 1] : 1.f;
-      acc[j][0] = fmaf(sacc[j][0], f0, acc[j][0]);
-      acc[j][1] = fmaf(sacc[j][1], f1, acc[j][1]);
-      acc[j][2] = fmaf(sacc[j][2], f0, acc[j][2]);
-      acc[j][3] = fmaf(sacc[j][3], f1, acc[j][3]);
+      for (int j = 0; j < NT; ++j) {
+        const float f0 = sinv[8 * j + 2 * t], f1 = sinv[8 * j + 2 * t + 1];
+        acc[j][0] = fmaf(sacc[j][0], f0, acc[j][0]);
+        acc[j][1] = fmaf(sacc[j][1], f1, acc[j][1]);
+        acc[j][2] = fmaf(sacc[j][2], f0, acc[j][2]);
+        acc[j][3] = fmaf(sacc[j][3], f1, acc[j][3]);
+      }
     }
     if (++slot == STAGES) slot = 0, ph ^= 1u;
   }
@@ -574,11 +589,29 @@ static int32_t launch_sk(const LinearArgs &a, int sk, int splits, float *ws, uns
   return b200_set_error(B200_ERR_UNSUPPORTED, "skinny GEMM: scale layout");
 }
 
+// The 64-token tile serves 33..64 tokens for the scale layouts the tcgen05 GEMM declines (per-32
+// fp16 / bf16 / fp32 scales and wider group scales, which it cannot fold into its operand exactly).
+static bool wide_tile_scales(int sk) {
+  return sk == SK_F16 || sk == SK_BF16 || sk == SK_F32 || sk == SK_GROUP;
+}
+
+template <int FMT>
+static int32_t launch_sk64(const LinearArgs &a, int sk, int splits, float *ws, unsigned int *tk, cudaStream_t s) {
+  switch (sk) {
+    case SK_F16: return launch_x<FMT, 8, SK_F16>(a, splits, ws, tk, s);
+    case SK_BF16: return launch_x<FMT, 8, SK_BF16>(a, splits, ws, tk, s);
+    case SK_F32: return launch_x<FMT, 8, SK_F32>(a, splits, ws, tk, s);
+    case SK_GROUP: return launch_x<FMT, 8, SK_GROUP>(a, splits, ws, tk, s);
+  }
+  return b200_set_error(B200_ERR_UNSUPPORTED, "skinny GEMM: no 64-token tile for this scale layout");
+}
+
 template <int FMT>
 static int32_t launch_nt(const LinearArgs &a, int sk, int splits, float *ws, unsigned int *tk, cudaStream_t s) {
   if (a.m <= 8) return launch_sk<FMT, 1>(a, sk, splits, ws, tk, s);
   if (a.m <= 16) return launch_sk<FMT, 2>(a, sk, splits, ws, tk, s);
-  return launch_sk<FMT, 4>(a, sk, splits, ws, tk, s);
+  if (a.m <= 32) return launch_sk<FMT, 4>(a, sk, splits, ws, tk, s);
+  return launch_sk64<FMT>(a, sk, splits, ws, tk, s);
 }
 
 static int choose_splits(const LinearArgs &a, int sms) {
@@ -594,7 +627,8 @@ static int choose_splits(const LinearArgs &a, int sms) {
 
 bool skinny_supported(const LinearArgs &a) {
   using namespace skinny;
-  if (a.m < 3 || a.m > 32) return false;
+  if (a.m < 3 || a.m > 64) return false;
+  if (a.m > 32 && !wide_tile_scales(gemv::scale_kind(a))) return false;
   if (!(a.fmt == B200_FMT_INT4 || a.fmt == B200_FMT_UINT4 || a.fmt == B200_FMT_FP4_E2M1)) return false;
   if (a.xdt != B200_DT_F16 && a.xdt != B200_DT_BF16) return false;
   if (a.ydt != B200_DT_F16 && a.ydt != B200_DT_BF16 && a.ydt != B200_DT_F32) return false;
