@@ -185,6 +185,18 @@ def test_group_scales_decode_gemv(bs, scale, m, fmt):
     assert plan == "gemv"
 
 
+@pytest.mark.parametrize("rows,cols", [(4096, 14336), (4768, 4096), (4736, 4096), (320, 4096)])
+@pytest.mark.parametrize("bs,scale", [(64, "bfloat16"), (128, "float16"), (256, "float32"), (512, "float32")])
+@pytest.mark.parametrize("m", [1, 2])
+def test_group_scales_streamed_gemv(rows, cols, bs, scale, m):
+    """Group scales on the streamed decode GEMV (c4 projections use INT4 with fp16 group-128
+    scales): each stage stages a 16-byte-aligned box of group scales per row and indexes the
+    stage's groups inside it; both consumer-warp counts (4736 / 4768 rows)."""
+    spec = _spec("int4", rows, cols, bs, "f16u", 43)
+    plan, *_ = _run(spec, scale, m, "float16", "float16", "gemv")
+    assert plan == "gemv"
+
+
 @pytest.mark.parametrize("bs", [32, 128])
 def test_gemm_rejects_inexact_group_scales(bs):
     """Non-power-of-two group scales cannot be folded exactly into a 16-bit tcgen05 operand

@@ -10,7 +10,8 @@
 //   * persistent CTAs (as many per SM as fit); CTA c owns a contiguous range of 32-row blocks;
 //   * the last warp's lane 0 is a TMA producer: for each row block it streams 32 rows x 512
 //     payloads per stage (256 B/row for 4-bit, 384 B/row for 6-bit) plus the stage's per-32
-//     block scales into a shared-memory ring (~80 KB in flight per CTA, no registers),
+//     block scales (or a 16-byte box of its 64..512-payload group scales) into a shared-memory
+//     ring (~80 KB in flight per CTA, no registers),
 //     signalled by mbarrier transaction counts; it starts before the programmatic-dependency
 //     wait because weights and scales are parameters, not outputs of the previous kernel;
 //   * warps 0-7 (0-15 when no CTA takes more than one row block) consume: four warps per
@@ -68,6 +69,14 @@ __host__ __device__ constexpr int scale_esz() {
 __device__ __forceinline__ float e8m0_fast(uint32_t b) {
   const uint32_t bits = b == 0xFFu ? 0x7FC00000u : max(b << 23, 0x00400000u);
   return __uint_as_float(bits);
+}
+
+template <int SK>
+__device__ __forceinline__ float smem_scale(const uint8_t *s) {
+  if constexpr (SK == SK_F16) return __half2float(*reinterpret_cast<const __half *>(s));
+  else if constexpr (SK == SK_BF16) return __uint_as_float((uint32_t)*reinterpret_cast<const uint16_t *>(s) << 16);
+  else if constexpr (SK == SK_F32) return *reinterpret_cast<const float *>(s);
+  else return 1.f;
 }
 
 template <int SK>
@@ -161,6 +170,12 @@ struct StreamParams {
   int64_t nrb;  // row blocks
   int nst;      // stages per row block
   int xbf16;
+  // Staged scales: gshift = log2(block / 32) (0: one scale per 32-payload block; 1..4: group
+  // scales of 64..512 payloads). Each stage loads a box of sbe scales per row that starts at a
+  // multiple of sbe, since a TMA box is at least 16 bytes wide (four fp16 group-128 scales
+  // are 8): the stage's first scale sits at offset (st * (16 >> gshift)) % sbe of the box.
+  int gshift, sbe;
+  uint32_t tx;  // bytes per stage (codes + scale box)
 };
 
 // stage x[m][K] as fp16 in decode pair order (consumer threads only). Each thread issues up to
@@ -214,7 +229,7 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"r"(NC * 32) : "memory");
 }
 
-template <int FMT, int SK, int NC>
+template <int FMT, int SK, int NC, bool GS>
 __global__ void __launch_bounds__(threads<NC>(), 1)
     gemv_stream_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tms,
                        StreamParams sp) {
@@ -266,7 +281,7 @@ __global__ void __launch_bounds__(threads<NC>(), 1)
           if (gs >= STAGES && !mbar_wait(&empty[slot], round ^ 1u, abort_flag)) continue;
           if (*abort_flag) continue;
           uint8_t *dst = ring + slot * SLOT;
-          mbar_arrive_expect_tx(&full[slot], TX);
+          mbar_arrive_expect_tx(&full[slot], GS ? sp.tx : TX);
           if constexpr (BITS == 4) {
             tma_load_2d(dst, &tmw, st * WR, (int32_t)(rbk * RB), &full[slot]);
           } else {  // 384 B per row: two 192-byte boxes
@@ -274,7 +289,8 @@ __global__ void __launch_bounds__(threads<NC>(), 1)
             tma_load_2d(dst + RB * (WR / 2), &tmw, st * WR + WR / 2, (int32_t)(rbk * RB), &full[slot]);
           }
           if constexpr (GROUP)
-            tma_load_2d(dst + RB * WR, &tms, st * (KSTAGE / 32), (int32_t)(rbk * RB), &full[slot]);
+            tma_load_2d(dst + RB * WR, &tms, GS ? (st * (16 >> sp.gshift)) & ~(sp.sbe - 1) : st * (KSTAGE / 32),
+                        (int32_t)(rbk * RB), &full[slot]);
         }
       }
       if (*abort_flag) {  // drain copies still in flight before exiting
@@ -352,11 +368,19 @@ __global__ void __launch_bounds__(threads<NC>(), 1)
           }
         } else if constexpr (GROUP) {
           const uint8_t *sb = base + RB * WR;
-          const int blk = sub * 4 + cblk;  // block index within the stage's 16 blocks per row
-          smem_scale_pair<SK>(sb + (g * (KSTAGE / 32) + blk) * SESZ, r.lo.sa0, r.lo.sa1);
-          smem_scale_pair<SK>(sb + ((g + 8) * (KSTAGE / 32) + blk) * SESZ, r.lo.sb0, r.lo.sb1);
-          smem_scale_pair<SK>(sb + ((g + 16) * (KSTAGE / 32) + blk) * SESZ, r.hi.sa0, r.hi.sa1);
-          smem_scale_pair<SK>(sb + ((g + 24) * (KSTAGE / 32) + blk) * SESZ, r.hi.sb0, r.hi.sb1);
+          const int blk = sub * 4 + cblk;  // block index within the stage's 16 blocks per row (even)
+          if constexpr (!GS) {
+            smem_scale_pair<SK>(sb + (g * (KSTAGE / 32) + blk) * SESZ, r.lo.sa0, r.lo.sa1);
+            smem_scale_pair<SK>(sb + ((g + 8) * (KSTAGE / 32) + blk) * SESZ, r.lo.sb0, r.lo.sb1);
+            smem_scale_pair<SK>(sb + ((g + 16) * (KSTAGE / 32) + blk) * SESZ, r.hi.sa0, r.hi.sa1);
+            smem_scale_pair<SK>(sb + ((g + 24) * (KSTAGE / 32) + blk) * SESZ, r.hi.sb0, r.hi.sb1);
+          } else {  // blocks blk, blk + 1 share one group scale
+            const int gi = ((st * (16 >> sp.gshift)) & (sp.sbe - 1)) + (blk >> sp.gshift);
+            r.lo.sa0 = r.lo.sa1 = smem_scale<SK>(sb + (g * sp.sbe + gi) * SESZ);
+            r.lo.sb0 = r.lo.sb1 = smem_scale<SK>(sb + ((g + 8) * sp.sbe + gi) * SESZ);
+            r.hi.sa0 = r.hi.sa1 = smem_scale<SK>(sb + ((g + 16) * sp.sbe + gi) * SESZ);
+            r.hi.sb0 = r.hi.sb1 = smem_scale<SK>(sb + ((g + 24) * sp.sbe + gi) * SESZ);
+          }
         }
       }
       __syncwarp();
@@ -398,20 +422,24 @@ static size_t smem_bytes(int64_t m, int64_t cols) {
          2 * NC * 2 * RB * 4 + CHUNK * 2 + (size_t)m * cols * 2;
 }
 
-template <int FMT, int SK, int NC>
+template <int FMT, int SK, int NC, bool GS>
 static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
   constexpr int BITS = Fmt<FMT>::bits;
   constexpr int SESZ = scale_esz<SK>();
   const size_t smem = smem_bytes<BITS, SESZ, NC>(a.m, a.cols);
   int sms = 0;
   B200_CUDA_TRY(device_sms(&sms));
-  B200_CUDA_TRY((ensure_dynamic_smem<gemv_stream_kernel<FMT, SK, NC>>(200 * 1024)));
+  B200_CUDA_TRY((ensure_dynamic_smem<gemv_stream_kernel<FMT, SK, NC, GS>>(200 * 1024)));
   int per_sm = 0;
   B200_CUDA_TRY(
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stream_kernel<FMT, SK, NC>, threads<NC>(), smem));
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stream_kernel<FMT, SK, NC, GS>, threads<NC>(), smem));
   if (per_sm < 1) return b200_set_error(B200_ERR_UNSUPPORTED, "streamed GEMV: no CTA fits (%zu B smem)", smem);
   CUtensorMap tmw, tms;
   const uint64_t row_bytes = (uint64_t)a.cols * BITS / 8;
+  int gshift = 0;  // group scales: block = 32 << gshift payloads
+  while (GS && (32 << gshift) < a.block) ++gshift;
+  const int gps = (KSTAGE / 32) >> gshift;  // scales per row and stage
+  const int sbe = gshift == 0 ? KSTAGE / 32 : (gps * SESZ >= 16 ? gps : 16 / (SESZ > 0 ? SESZ : 1));
   if (int32_t rc = make_tma_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, row_bytes, (uint64_t)a.rows, row_bytes,
                                BITS == 4 ? wrow<BITS>() : wrow<BITS>() / 2, RB, CU_TENSOR_MAP_SWIZZLE_NONE))
     return rc;
@@ -421,7 +449,7 @@ static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
                                    : SK == SK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     if (int32_t rc = make_tma_2d(&tms, dt, a.scales, (uint64_t)a.nblk, (uint64_t)a.rows, (uint64_t)a.nblk * SESZ,
-                                 KSTAGE / 32, RB, CU_TENSOR_MAP_SWIZZLE_NONE))
+                                 (uint32_t)sbe, RB, CU_TENSOR_MAP_SWIZZLE_NONE))
       return rc;
   } else {
     tms = tmw;
@@ -436,6 +464,9 @@ static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
   sp.nrb = (a.rows + RB - 1) / RB;
   sp.nst = (int)(a.cols / KSTAGE);
   sp.xbf16 = a.xdt == B200_DT_BF16;
+  sp.gshift = gshift;
+  sp.sbe = sbe;
+  sp.tx = (uint32_t)(RB * wrow<BITS>() + RB * sbe * SESZ);
   const int64_t slots = (int64_t)sms * per_sm;
   const int64_t grid = sp.nrb < slots ? sp.nrb : slots;
   cudaLaunchConfig_t cfg = {};
@@ -448,7 +479,7 @@ static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
   attrs[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = (a.flags & B200_FLAG_PDL) ? 1 : 0;
-  B200_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stream_kernel<FMT, SK, NC>, tmw, tms, sp));
+  B200_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_stream_kernel<FMT, SK, NC, GS>, tmw, tms, sp));
   return B200_OK;
 }
 
@@ -456,14 +487,16 @@ static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
 // bound and twice the warps halve its stage rounds (FP4, M=1: 1280 x 8192 8.7 -> 6.4 us,
 // 4096 x 4096 5.8 -> 4.3 us). CTAs that stream several row blocks keep 8 (16 measured slower:
 // 8192 x 8192 10.5 -> 11.4 us, 28672 x 8192 28.9 -> 34 us).
-template <int FMT, int SK>
+// GS: group scales (block 64..512) in the per-dtype kernels; a separate instantiation keeps the
+// per-32 kernels' registers (and two CTAs per SM) as they are
+template <int FMT, int SK, bool GS = false>
 static int32_t launch_nc(const LinearArgs &a, cudaStream_t stream) {
   int sms = 0;
   B200_CUDA_TRY(device_sms(&sms));
   const int64_t nrb = (a.rows + RB - 1) / RB;
   if (nrb <= sms && smem_bytes<Fmt<FMT>::bits, scale_esz<SK>(), 16>(a.m, a.cols) <= 200 * 1024)
-    return launch_t<FMT, SK, 16>(a, stream);
-  return launch_t<FMT, SK, 8>(a, stream);
+    return launch_t<FMT, SK, 16, GS>(a, stream);
+  return launch_t<FMT, SK, 8, GS>(a, stream);
 }
 
 template <int FMT>
@@ -475,6 +508,10 @@ static int32_t dispatch_sk(const LinearArgs &a, int sk, cudaStream_t stream) {
     case SK_F16: return launch_nc<FMT, SK_F16>(a, stream);
     case SK_BF16: return launch_nc<FMT, SK_BF16>(a, stream);
     case SK_F32: return launch_nc<FMT, SK_F32>(a, stream);
+    case SK_GROUP:  // the per-dtype kernels with gshift > 0
+      return a.sdt == B200_DT_F16    ? launch_nc<FMT, SK_F16, true>(a, stream)
+             : a.sdt == B200_DT_BF16 ? launch_nc<FMT, SK_BF16, true>(a, stream)
+                                     : launch_nc<FMT, SK_F32, true>(a, stream);
   }
   return b200_set_error(B200_ERR_UNSUPPORTED, "streamed GEMV: scale layout");
 }
@@ -486,10 +523,12 @@ bool gemv_stream_supported(const LinearArgs &a) {
   if (!gemv_tc_supported(a)) return false;
   if (a.cols % KSTAGE != 0 || a.cols > (1 << 24)) return false;
   const int sk = gemv::scale_kind(a);
-  // group scales wider than 32 (block 64..512) go to the register-ring GEMV, which prefetches
-  // them with the weights (a variant of this kernel loading one scale per row and chunk from
-  // global memory measured slower: c4 stack 4.7 vs 2.6 ms per token)
-  if (sk == gemv::SK_GROUP) return false;
+  // group scales wider than 32 (block 64..512): staged per stage like per-32 scales (a TMA box
+  // of at least 16 bytes per row); E8M0 group scales stay on the register-ring GEMV
+  if (sk == gemv::SK_GROUP) {
+    if (!(a.sdt == B200_DT_F16 || a.sdt == B200_DT_BF16 || a.sdt == B200_DT_F32)) return false;
+    if (!(a.block == 64 || a.block == 128 || a.block == 256 || a.block == 512)) return false;
+  }
   if (sk >= gemv::SK_E8M0) {
     const int esz = dt_size(a.sdt);
     if ((a.nblk * esz) % 16 != 0 || (uintptr_t)a.scales % 16 != 0) return false;
