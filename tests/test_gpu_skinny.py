@@ -40,7 +40,7 @@ def _check(spec, scale_dtype, m, xdt, ydt, x=None, seed=1):
 
 SCALES = [(None, 32, None), ("f16row", 0, None), ("e8m0", 32, "e8m0"), ("e8m0", 32, "bfloat16"),
           ("f16u", 32, "float16"), ("f16u", 32, "float32"), ("f16u", 64, "float16"), ("f16u", 128, "float16"),
-          ("f16u", 512, "bfloat16")]
+          ("f16u", 512, "bfloat16"), ("f16u", 128, "float32"), ("f16u", 64, "float32"), ("e8m0", 128, "e8m0")]
 
 
 @pytest.mark.parametrize("fmt", ["int4", "uint4", "fp4_e2m1"])

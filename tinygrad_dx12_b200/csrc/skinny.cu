@@ -84,9 +84,16 @@ __host__ __device__ constexpr int stages(int esz) {
                                                      : smem_cap<NT>() / slot_bytes<NT>(esz);
 }
 
+// Group scales (64..512 payloads, fp16 / bf16 / fp32) staged like the per-32 kinds: per stage
+// one 16-byte box of scales per row (TMA boxes are at least 16 bytes wide; four fp16 group-128
+// scales are 8), starting at a multiple of the box; the stage's groups begin at offset
+// (stage * groups per stage) mod box. SK_GROUP reads group scales from global memory instead
+// (other shapes: E8M0 groups, scale rows that are not 16-byte multiples, fp32 group-64).
+constexpr int SK_GSTAGED = 16;
+
 template <int SK>
-__host__ __device__ constexpr int tile_esz() {  // scale bytes staged per element (per-32 kinds)
-  return SK == SK_E8M0 ? 1 : SK == SK_F16 || SK == SK_BF16 ? 2 : SK == SK_F32 ? 4 : 0;
+__host__ __device__ constexpr int tile_esz() {  // staged scale bytes per 32-payload block and row
+  return SK == SK_E8M0 || SK == SK_GSTAGED ? 1 : SK == SK_F16 || SK == SK_BF16 ? 2 : SK == SK_F32 ? 4 : 0;
 }
 
 struct SkParams {
@@ -101,6 +108,7 @@ struct SkParams {
   int64_t ldy_m, ldy_n;
   int64_t rows;
   int nst;       // stages along K
+  int gps, gbox;  // SK_GSTAGED: group scales per stage and row, scales per 16-byte box
   int splits;    // K slices
   int xbf16;
   float *ws;     // [splits][m][rows] fp32 partials (splits > 1)
@@ -182,14 +190,16 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
     skinny_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
                   const __grid_constant__ CUtensorMap tms, SkParams p) {
   constexpr int ESZ = tile_esz<SK>();
-  constexpr bool TILE_SCALES = ESZ > 0;
+  constexpr bool STAGE_SCALES = ESZ > 0;                        // TMA stages a scale tile
+  constexpr bool TILE_SCALES = STAGE_SCALES && SK != SK_GSTAGED;  // per-32 scales
+  constexpr bool GROUPED = SK == SK_GROUP || SK == SK_GSTAGED;
   constexpr int SLOT = slot_bytes<NT>(ESZ);
   constexpr int STAGES = stages<NT>(ESZ);
   constexpr int TOK = 8 * NT;
   constexpr int NC = consumers<NT, SK>();
   constexpr int KH = NC / 8;         // warps per row group; each takes 1/KH of a stage's blocks
   constexpr int NB = KST / 32 / KH;  // 32-payload blocks per warp and stage
-  constexpr uint32_t TX = W_BYTES + x_bytes<NT>() + (TILE_SCALES ? s_bytes(ESZ) : 0);
+  constexpr uint32_t TX = W_BYTES + x_bytes<NT>() + (STAGE_SCALES ? s_bytes(ESZ) : 0);
   extern __shared__ uint8_t smem_raw[];
   uint8_t *ring = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t *full = reinterpret_cast<uint64_t *>(ring + STAGES * SLOT);
@@ -218,7 +228,7 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
     if (lane == 0) {
       prefetch_tmap(&tmw);
       prefetch_tmap(&tmx);
-      if constexpr (TILE_SCALES) prefetch_tmap(&tms);
+      if constexpr (STAGE_SCALES) prefetch_tmap(&tms);
       int slot = 0, issued = 0;
       uint32_t ph = 0;
       for (int st = st0; st < st1; ++st) {
@@ -230,8 +240,9 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
         tma_load_2d(dst + RB * 128, &tmw, st * (KST / 2) + 128, rblk * RB, &full[slot]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) tma_load_2d(dst + W_BYTES + j * (TOK * 128), &tmx, st * KST + 64 * j, 0, &full[slot]);
-        if constexpr (TILE_SCALES)
-          tma_load_2d(dst + W_BYTES + x_bytes<NT>(), &tms, st * (KST / 32), rblk * RB, &full[slot]);
+        if constexpr (STAGE_SCALES)
+          tma_load_2d(dst + W_BYTES + x_bytes<NT>(), &tms,
+                      SK == SK_GSTAGED ? (st * p.gps) & ~(p.gbox - 1) : st * (KST / 32), rblk * RB, &full[slot]);
         ++issued;
         if (++slot == STAGES) slot = 0, ph ^= 1u;
       }
@@ -323,7 +334,7 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
                  __vcmpleu4(e8h[i], 0x8B8B8B8Bu);
         e8fast = __all_sync(0xffffffffu, inr == 0xFFFFFFFFu);
       }
-      float gd[NT][4];  // running partial of the current scale group (SK_GROUP)
+      float gd[NT][4];  // running partial of the current scale group (group kinds)
 #pragma unroll
       for (int j = 0; j < NT; ++j) gd[j][0] = gd[j][1] = gd[j][2] = gd[j][3] = 0.f;
 #pragma unroll
@@ -378,7 +389,7 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
               sacc[j][1] = fmaf(d[1], sl, sacc[j][1]);
               sacc[j][2] = fmaf(d[2], sh, sacc[j][2]);
               sacc[j][3] = fmaf(d[3], sh, sacc[j][3]);
-            } else if constexpr (SK == SK_GROUP) {
+            } else if constexpr (GROUPED) {
               mma16816(gd[j], a0, xv.x, xv.y);
               mma16816(gd[j], a1, xv.z, xv.w);
             } else {
@@ -386,9 +397,16 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
               mma16816(sacc[j], a1, xv.z, xv.w);
             }
           }
-          if constexpr (SK == SK_GROUP) {
+          if constexpr (GROUPED) {
             if (((32 * (bb + 1)) & (p.block - 1)) == 0) {  // the group ends with this block
-              const float gl = sgl[2 * jp + h], gh = sgh[2 * jp + h];
+              float gl, gh;
+              if constexpr (SK == SK_GSTAGED) {
+                const int e = ((st * p.gps) & (p.gbox - 1)) + ((bb + 1) >> (p.block_log2 - 5)) - 1;
+                gl = load_as_f32(srow_lo, e, p.sdt);
+                gh = load_as_f32(srow_hi, e, p.sdt);
+              } else {
+                gl = sgl[2 * jp + h], gh = sgh[2 * jp + h];
+              }
 #pragma unroll
               for (int j = 0; j < NT; ++j) {
                 sacc[j][0] = fmaf(gd[j][0], gl, sacc[j][0]);
@@ -542,7 +560,15 @@ static int32_t launch_t(const LinearArgs &a, int splits, float *ws, unsigned int
                                (uint64_t)a.cols, (uint64_t)a.m, (uint64_t)a.ldx * 2, 64, 8 * NT,
                                CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
-  if constexpr (ESZ > 0) {
+  if constexpr (SK == SK_GSTAGED) {
+    const int esz = dt_size(a.sdt);
+    const CUtensorMapDataType dt = a.sdt == B200_DT_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : a.sdt == B200_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if (int32_t rc = make_tma_2d(&tms, dt, a.scales, (uint64_t)a.nblk, (uint64_t)a.rows, (uint64_t)a.nblk * esz,
+                                 (uint32_t)(16 / esz), RB, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+  } else if constexpr (ESZ > 0) {
     const CUtensorMapDataType dt = ESZ == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
                                    : ESZ == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                    : SK == SK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -557,6 +583,8 @@ static int32_t launch_t(const LinearArgs &a, int splits, float *ws, unsigned int
   p.scales = a.scales, p.sdt = a.sdt, p.nblk = a.nblk, p.block = a.block;
   p.block_log2 = 0;
   while (((int64_t)1 << p.block_log2) < a.block) ++p.block_log2;
+  p.gps = (int)(KST / (a.block > 0 ? a.block : KST));
+  p.gbox = SK == SK_GSTAGED ? 16 / dt_size(a.sdt) : 1;
   p.x = a.x, p.m = a.m, p.y = a.y, p.ydt = a.ydt, p.ldy_m = a.ldy_m, p.ldy_n = a.ldy_n, p.rows = a.rows;
   p.nst = (int)(a.cols / KST);
   p.splits = splits;
@@ -575,6 +603,14 @@ static int32_t launch_x(const LinearArgs &a, int splits, float *ws, unsigned int
                                : launch_t<FMT, NT, SK, false>(a, splits, ws, tk, s);
 }
 
+// Group scales that fit the staged layout: fp16 / bf16 / fp32, a stage's groups within one
+// 16-byte box, 16-byte scale rows and base.
+static bool group_staged(const LinearArgs &a) {
+  if (!(a.sdt == B200_DT_F16 || a.sdt == B200_DT_BF16 || a.sdt == B200_DT_F32)) return false;
+  const int esz = dt_size(a.sdt);
+  return (KST / a.block) * esz <= 16 && (a.nblk * esz) % 16 == 0 && (uintptr_t)a.scales % 16 == 0;
+}
+
 template <int FMT, int NT>
 static int32_t launch_sk(const LinearArgs &a, int sk, int splits, float *ws, unsigned int *tk, cudaStream_t s) {
   switch (sk) {
@@ -584,7 +620,9 @@ static int32_t launch_sk(const LinearArgs &a, int sk, int splits, float *ws, uns
     case SK_F16: return launch_x<FMT, NT, SK_F16>(a, splits, ws, tk, s);
     case SK_BF16: return launch_x<FMT, NT, SK_BF16>(a, splits, ws, tk, s);
     case SK_F32: return launch_x<FMT, NT, SK_F32>(a, splits, ws, tk, s);
-    case SK_GROUP: return launch_x<FMT, NT, SK_GROUP>(a, splits, ws, tk, s);
+    case SK_GROUP:
+      return group_staged(a) ? launch_x<FMT, NT, SK_GSTAGED>(a, splits, ws, tk, s)
+                             : launch_x<FMT, NT, SK_GROUP>(a, splits, ws, tk, s);
   }
   return b200_set_error(B200_ERR_UNSUPPORTED, "skinny GEMM: scale layout");
 }
@@ -601,7 +639,9 @@ static int32_t launch_sk64(const LinearArgs &a, int sk, int splits, float *ws, u
     case SK_F16: return launch_x<FMT, 8, SK_F16>(a, splits, ws, tk, s);
     case SK_BF16: return launch_x<FMT, 8, SK_BF16>(a, splits, ws, tk, s);
     case SK_F32: return launch_x<FMT, 8, SK_F32>(a, splits, ws, tk, s);
-    case SK_GROUP: return launch_x<FMT, 8, SK_GROUP>(a, splits, ws, tk, s);
+    case SK_GROUP:
+      return group_staged(a) ? launch_x<FMT, 8, SK_GSTAGED>(a, splits, ws, tk, s)
+                             : launch_x<FMT, 8, SK_GROUP>(a, splits, ws, tk, s);
   }
   return b200_set_error(B200_ERR_UNSUPPORTED, "skinny GEMM: no 64-token tile for this scale layout");
 }
