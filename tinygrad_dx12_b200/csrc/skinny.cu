@@ -486,15 +486,17 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
       const int64_t m = 8 * j + 2 * t + (i & 1), n = i < 2 ? nlo : nhi;
       if (kh == 0 && m < p.m && n < p.rows) p.ws[((int64_t)split * p.m + m) * p.rows + n] = acc[j][i];
     }
-  __threadfence();
+  // one thread publishes the CTA's partials (the barrier orders every thread's stores before its
+  // release) and, if it is the last slice, acquires the others' (the barrier after it orders the
+  // reads below): cheaper than a full fence in every thread
   consumer_sync<NC>();
   if (tid == 0) {
-    const unsigned int ticket = atomicAdd(&p.tickets[rblk], 1u);
+    unsigned int ticket;
+    asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(ticket) : "l"(&p.tickets[rblk]) : "memory");
     *last_flag = ticket == (unsigned int)(p.splits - 1);
   }
   consumer_sync<NC>();
   if (!*last_flag) return;
-  __threadfence();
   const int64_t n0 = (int64_t)rblk * RB;
   for (int e = tid; e < RB * (int)p.m; e += NC * 32) {
     const int64_t m = e / RB, n = n0 + e % RB;
