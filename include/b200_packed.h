@@ -78,7 +78,8 @@ extern "C" {
  * the previous kernel on the stream is still running; it streams its packed weights and
  * scales at once and waits for that kernel before it reads x or writes y. Only valid when
  * the weights and scales are not written by the immediately preceding kernels (true for
- * inference weights); the activation dependency is always honoured. */
+ * inference weights); the activation dependency is always honoured. Honoured by the decode
+ * GEMV (M <= 2) and the decode GEMM for 3..64 tokens; the other kernels ignore it. */
 #define B200_FLAG_PDL 0x100
 
 /*

@@ -222,6 +222,7 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
     fence_mbar_init();
   }
   __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == NC) {
     // ---------------- TMA producer ----------------
@@ -229,20 +230,31 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
       prefetch_tmap(&tmw);
       prefetch_tmap(&tmx);
       if constexpr (STAGE_SCALES) prefetch_tmap(&tms);
-      int slot = 0, issued = 0;
-      uint32_t ph = 0;
-      for (int st = st0; st < st1; ++st) {
-        if (issued >= STAGES && !mbar_wait(&empty[slot], ph ^ 1u, abort_flag)) break;
-        if (*abort_flag) break;
+      // codes and scales are parameters: the first ring's worth is requested before the
+      // programmatic-dependency wait (x may be the previous kernel's output)
+      auto load_wscales = [&](int st, int slot) {
         uint8_t *dst = ring + slot * SLOT;
         mbar_arrive_expect_tx(&full[slot], TX);
         tma_load_2d(dst, &tmw, st * (KST / 2), rblk * RB, &full[slot]);
         tma_load_2d(dst + RB * 128, &tmw, st * (KST / 2) + 128, rblk * RB, &full[slot]);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) tma_load_2d(dst + W_BYTES + j * (TOK * 128), &tmx, st * KST + 64 * j, 0, &full[slot]);
         if constexpr (STAGE_SCALES)
           tma_load_2d(dst + W_BYTES + x_bytes<NT>(), &tms,
                       SK == SK_GSTAGED ? (st * p.gps) & ~(p.gbox - 1) : st * (KST / 32), rblk * RB, &full[slot]);
+      };
+      const int pre = st1 - st0 < STAGES ? st1 - st0 : STAGES;
+      for (int i = 0; i < pre; ++i) load_wscales(st0 + i, i);
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      int slot = 0, issued = 0;
+      uint32_t ph = 0;
+      for (int st = st0; st < st1; ++st) {
+        if (issued >= pre) {
+          if (issued >= STAGES && !mbar_wait(&empty[slot], ph ^ 1u, abort_flag)) break;
+          if (*abort_flag) break;
+          load_wscales(st, slot);
+        }
+        uint8_t *dst = ring + slot * SLOT;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) tma_load_2d(dst + W_BYTES + j * (TOK * 128), &tmx, st * KST + 64 * j, 0, &full[slot]);
         ++issued;
         if (++slot == STAGES) slot = 0, ph ^= 1u;
       }
@@ -259,6 +271,8 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
   }
 
   // ---------------- consumers ----------------
+  // x, y and the split-K workspace belong to the stream order: wait for the previous kernel
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int g = lane >> 2, t = lane & 3;
   const int kh = KH == 1 ? 0 : warp / 8;  // which part of each stage's blocks this warp takes
   const int r0 = (KH == 1 ? warp : warp % 8) * 16;  // rows r0 + g, r0 + g + 8 (within the CTA's 128)
@@ -597,8 +611,17 @@ static int32_t launch_t(const LinearArgs &a, int splits, float *ws, unsigned int
   p.ws = ws;
   p.tickets = tickets;
   const int64_t nrb = (a.rows + RB - 1) / RB;
-  skinny_kernel<FMT, NT, SK, XBF16><<<(unsigned)(nrb * splits), threads<NT, SK>(), smem, stream>>>(tmw, tmx, tms, p);
-  B200_LAUNCH_CHECK();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(nrb * splits));
+  cfg.blockDim = dim3(threads<NT, SK>());
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = (a.flags & B200_FLAG_PDL) ? 1 : 0;
+  B200_CUDA_TRY(cudaLaunchKernelEx(&cfg, skinny_kernel<FMT, NT, SK, XBF16>, tmw, tmx, tms, p));
   return B200_OK;
 }
 

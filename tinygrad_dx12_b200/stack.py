@@ -34,7 +34,7 @@ from . import dtypes as D
 from .packed import FORMATS, PackedTensor, stream_ptr
 
 EPS = 1e-6
-FLAG_PDL = 0x100  # B200_FLAG_PDL: the decode GEMV may start streaming weights while the previous kernel ends
+FLAG_PDL = 0x100  # B200_FLAG_PDL: the decode kernels (M <= 64) may start streaming weights while the previous kernel ends
 
 
 @dataclasses.dataclass(frozen=True)
@@ -167,7 +167,7 @@ class CudaOps:
     def linear(self, w: PackedTensor, x: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
         from .linalg import _packed_linear
 
-        return _packed_linear(w, x, out_dtype, "auto", FLAG_PDL if x.shape[0] <= 2 else 0)
+        return _packed_linear(w, x, out_dtype, "auto", FLAG_PDL if x.shape[0] <= 64 else 0)
 
     def add_rmsnorm(self, h: torch.Tensor, partial: torch.Tensor | None, x_out: torch.Tensor | None) -> None:
         _lib.call("b200_add_rmsnorm", h.data_ptr(), _lib.DT[D.name(h.dtype)],
@@ -287,7 +287,7 @@ class PeerOps(CudaOps):
         if h.shape[0] > self.reducer.rows_max:  # beyond the shared buffers: NCCL all-reduce
             return super().row_reduce(w, inp, h, x, slot)
         _packed_linear_multi(w, inp, self.reducer.push_targets(slot), torch.float32, h.shape[1],
-                             FLAG_PDL if inp.shape[0] <= 2 else 0)
+                             FLAG_PDL if inp.shape[0] <= 64 else 0)
         self.reducer.reduce(slot, h, x)
 
     def close(self) -> None:
