@@ -76,7 +76,7 @@ def test_bf16_prescale(mag):
 
 @pytest.mark.parametrize("exps", [(-20, -15), (10, 20), (-3, 3)])
 def test_e8m0_exponent_ranges(exps):
-    """E8M0 scales inside and outside the range the kernel folds into fp16 weights."""
+    """E8M0 scales of small, large and mixed exponents (each block's fp32 sum is scaled)."""
     rng = np.random.default_rng(5)
     spec = ref.make_packed(rng, "fp4_e2m1", 256, 2048, 32, None)
     e = rng.integers(exps[0], exps[1] + 1, size=(256, 64))

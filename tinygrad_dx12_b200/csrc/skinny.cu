@@ -326,8 +326,9 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
       const uint8_t *srow_hi = srow_lo + 8 * (KST / 32) * ESZ;
       const uint32_t wbase = smem_u32(base);
       // the E8M0 scales of this warp's NB blocks, rows g / g+8 (word i holds local blocks 4i..4i+3)
+      // (applied to each block's fp32 MMA result: folding them into the fp16 operand with HMUL2
+      // measured slower on every tile, FP4 8192^2 M=8 20.98 vs 20.03 us, M=32 fp16 x 32.7 vs 29.5)
       uint32_t e8l[SK == SK_E8M0 ? NB / 4 : 1] = {}, e8h[SK == SK_E8M0 ? NB / 4 : 1] = {};
-      bool e8fast = false;
       if constexpr (SK == SK_E8M0) {
         if constexpr (NB == 16) {
           const uint4 ul = *reinterpret_cast<const uint4 *>(srow_lo), uh = *reinterpret_cast<const uint4 *>(srow_hi);
@@ -338,18 +339,6 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
           const uint2 uh = *reinterpret_cast<const uint2 *>(srow_hi + kh * NB);
           e8l[0] = ul.x, e8l[1] = ul.y, e8h[0] = uh.x, e8h[1] = uh.y;
         }
-        // a normal fp16 2^e with e in [-14, 12] multiplies every decoded 4-bit payload exactly
-        // (at most two significant bits, 0.5 <= |value| <= 8: products stay within fp16, down to
-        // its subnormal quantum 2^-24): E8M0 bytes 113..139
-        uint32_t inr = 0xFFFFFFFFu;
-#pragma unroll
-        for (int i = 0; i < NB / 4; ++i)
-          inr &= __vcmpgeu4(e8l[i], 0x71717171u) & __vcmpleu4(e8l[i], 0x8B8B8B8Bu) & __vcmpgeu4(e8h[i], 0x71717171u) &
-                 __vcmpleu4(e8h[i], 0x8B8B8B8Bu);
-        // (the 8- and 16-token tiles scale each block's fp32 MMA result instead: 4 * NT FMAs per
-        // block against eight HMUL2 on the operand; FP4 8192^2: M=8 20.98 -> 20.03 us, M=16 fp16
-        // x 25.3 -> 23.7 us)
-        e8fast = NT > 2 && __all_sync(0xffffffffu, inr == 0xFFFFFFFFu);
       }
       float gd[NT][4];  // running partial of the current scale group (group kinds)
 #pragma unroll
@@ -372,21 +361,8 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
           if constexpr (SK == SK_E8M0) {
             const int jb = 2 * jp + h;  // local block: compile-time word and byte
             const uint32_t bl = (e8l[jb >> 2] >> (8 * (jb & 3))) & 0xFFu, bh = (e8h[jb >> 2] >> (8 * (jb & 3))) & 0xFFu;
-            if (e8fast) {  // fp16 2^(b-127) = bits (b - 112) << 10, exact in range; both halves
-              const uint32_t hl = (bl - 112u) << 10, hh = (bh - 112u) << 10;
-              const __half2 s2l = __halves2half2(__ushort_as_half((unsigned short)hl), __ushort_as_half((unsigned short)hl));
-              const __half2 s2h = __halves2half2(__ushort_as_half((unsigned short)hh), __ushort_as_half((unsigned short)hh));
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const __half2 vl = __hmul2(*reinterpret_cast<const __half2 *>(&ol[i]), s2l);
-                const __half2 vh = __hmul2(*reinterpret_cast<const __half2 *>(&oh[i]), s2h);
-                ol[i] = *reinterpret_cast<const uint32_t *>(&vl);
-                oh[i] = *reinterpret_cast<const uint32_t *>(&vh);
-              }
-            } else {
-              sl = e8m0_val(bl);
-              sh = e8m0_val(bh);
-            }
+            sl = e8m0_val(bl);
+            sh = e8m0_val(bh);
           } else if constexpr (TILE_SCALES) {
             sl = tile_scale<SK>(srow_lo, bb);
             sh = tile_scale<SK>(srow_hi, bb);
@@ -395,10 +371,7 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
 #pragma unroll
           for (int j = 0; j < NT; ++j) {
             const uint4 xv = *reinterpret_cast<const uint4 *>(xs + xbox * (TOK * 128) + (8 * j) * 128 + xoff[bb & 1]);
-            if (SK == SK_E8M0 && e8fast) {
-              mma16816(sacc[j], a0, xv.x, xv.y);
-              mma16816(sacc[j], a1, xv.z, xv.w);
-            } else if constexpr (TILE_SCALES) {
+            if constexpr (TILE_SCALES) {
               float d[4] = {0.f, 0.f, 0.f, 0.f};
               mma16816(d, a0, xv.x, xv.y);
               mma16816(d, a1, xv.z, xv.w);
