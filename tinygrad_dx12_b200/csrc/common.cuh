@@ -230,5 +230,26 @@ inline cudaError_t ensure_dynamic_smem(int bytes) {
   return e;
 }
 
+// Resident CTAs per SM of kernel K (always launched with `threads` threads) at `smem` dynamic
+// bytes: the occupancy query costs about a microsecond of host time per launch, so the last
+// answer is kept per device (entry = 1 << 63 | smem << 8 | CTAs; thread-safe).
+template <auto K>
+inline cudaError_t occupancy_cached(int *per_sm, int threads, size_t smem) {
+  static std::atomic<uint64_t> cache[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::atomic<uint64_t> &slot = cache[dev & 63];
+  const uint64_t v = slot.load(std::memory_order_relaxed);
+  if ((v >> 63) && ((v >> 8) & 0xFFFFFFFFull) == smem) {
+    *per_sm = (int)(v & 0xFF);
+    return cudaSuccess;
+  }
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, K, threads, smem);
+  if (e == cudaSuccess && *per_sm >= 0 && *per_sm < 256 && smem < (1ull << 32))
+    slot.store((1ull << 63) | ((uint64_t)smem << 8) | (uint64_t)*per_sm, std::memory_order_relaxed);
+  return e;
+}
+
 }  // namespace b200
 

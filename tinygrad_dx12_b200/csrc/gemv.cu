@@ -431,8 +431,7 @@ static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
   B200_CUDA_TRY(device_sms(&sms));
   B200_CUDA_TRY((ensure_dynamic_smem<gemv_stream_kernel<FMT, SK, NC, GS>>(200 * 1024)));
   int per_sm = 0;
-  B200_CUDA_TRY(
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_stream_kernel<FMT, SK, NC, GS>, threads<NC>(), smem));
+  B200_CUDA_TRY((occupancy_cached<gemv_stream_kernel<FMT, SK, NC, GS>>(&per_sm, threads<NC>(), smem)));
   if (per_sm < 1) return b200_set_error(B200_ERR_UNSUPPORTED, "streamed GEMV: no CTA fits (%zu B smem)", smem);
   CUtensorMap tmw, tms;
   const uint64_t row_bytes = (uint64_t)a.cols * BITS / 8;
