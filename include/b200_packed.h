@@ -16,7 +16,7 @@
  *   - b200_last_error() copies the calling thread's last error message;
  *   - all pointers to tensors are device pointers owned by the caller. The compute entry
  *     points allocate nothing, with one exception: b200_packed_linear on a few tokens
- *     (3 <= m <= 32) splits K across CTAs and, on its first such call on a (device, stream),
+ *     (3 <= m <= 64) splits K across CTAs and, on its first such call on a (device, stream),
  *     allocates a 16 MiB split-K workspace kept for the life of the process
  *     (b200_packed_linear_noalloc is the allocation-free form). Other allocations are the
  *     explicit b200_malloc / b200_stream_create / b200_event_create calls;
