@@ -187,11 +187,15 @@ int32_t b200_packed_linear_multi(const b200_packed_desc *w, const void *x, int32
 /* Allocation-free form of b200_packed_linear for a few tokens (3 <= m <= 32, 4-bit formats,
  * the split-K decode GEMM). No counterpart in the reference. Same arguments and result as
  * b200_packed_linear with path B200_PATH_GEMV and unit k / n strides; bitwise the same result.
- * It never allocates device memory: its split-K scratch is a fixed 2 MiB device array of the
+ * It never calls an allocator: its split-K scratch is a fixed 2 MiB device array of the
  * library (per device), resolved on the first call on a device -- make that first call before
- * any stream capture. Shapes whose split-K partials would not fit (splits x m x N x 4 bytes
- * beyond the 2 MiB less 16 KiB of row-block tickets, or more than 4096 row blocks of 128
- * rows) return B200_ERR_UNSUPPORTED; shapes the kernel does not take return the same error.
+ * any stream capture. With CUDA's default lazy module loading, that first call (or any first
+ * call of this library's kernels) also loads the library's device code and commits the 2 MiB
+ * array on the device: make one warm-up call before the caller hands all free HBM to its own
+ * pool, or run the process with CUDA_MODULE_LOADING=EAGER. Shapes whose split-K partials
+ * would not fit (splits x m x N x 4 bytes beyond the 2 MiB less 16 KiB of row-block tickets,
+ * or more than 4096 row blocks of 128 rows; on a 148-SM B200 e.g. m = 32 with N >= 8192)
+ * return B200_ERR_UNSUPPORTED; shapes the kernel does not take return the same error.
  * Calls that overlap in time on one device (several streams or threads) share the array and
  * race: serialise them. */
 int32_t b200_packed_linear_noalloc(const b200_packed_desc *w, const void *x, int32_t x_dtype, int64_t m,

@@ -33,18 +33,22 @@ def rmsnorm(h: np.ndarray) -> np.ndarray:
     return h / np.sqrt(np.mean(h * h, axis=-1, keepdims=True, dtype=np.float32) + np.float32(EPS))
 
 
-def stack_forward(layers: list[dict], h0: np.ndarray, act: str) -> np.ndarray:
-    """layers: per layer a dict projection name -> PackedSpec (full matrices). Returns h (float32
-    array holding act-dtype values)."""
+def stack_forward(layers: list[dict], h0: np.ndarray, act: str, linear=None) -> np.ndarray:
+    """layers: a sequence (``len`` and indexing) holding per layer a dict projection name ->
+    PackedSpec (full matrices); a lazy sequence lets full-size layers be built one at a time.
+    ``linear(spec, x)`` computes x @ dequant(W)^T in float32 (default: the numpy restatement).
+    Returns h (float32 array holding act-dtype values)."""
+    linear = linear or ref.packed_linear_ref
     h = rnd(h0, act)
     x = rnd(rmsnorm(h), act)
-    for L in layers:
-        q = rnd(ref.packed_linear_ref(L["q"], x), act)
-        h = rnd(h + ref.packed_linear_ref(L["o"], q), act)
+    for i in range(len(layers)):
+        L = layers[i]
+        q = rnd(linear(L["q"], x), act)
+        h = rnd(h + linear(L["o"], q), act)
         x = rnd(rmsnorm(h), act)
-        g = rnd(ref.packed_linear_ref(L["gate"], x), act)
-        u = rnd(ref.packed_linear_ref(L["up"], x), act)
+        g = rnd(linear(L["gate"], x), act)
+        u = rnd(linear(L["up"], x), act)
         m = rnd(g * u, act)
-        h = rnd(h + ref.packed_linear_ref(L["down"], m), act)
+        h = rnd(h + linear(L["down"], m), act)
         x = rnd(rmsnorm(h), act)
     return h

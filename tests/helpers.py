@@ -77,3 +77,54 @@ def bits_equal(a: np.ndarray, b: np.ndarray) -> bool:
     a, b = np.ascontiguousarray(a), np.ascontiguousarray(b)
     return a.dtype.itemsize == b.dtype.itemsize and a.shape == b.shape and np.array_equal(
         a.view(np.uint8), b.view(np.uint8))
+
+
+_CLIB = None
+_C_FMT = {"int4": 0, "uint4": 1, "fp4_e2m1": 2, "fp6_e2m3": 3, "fp6_e3m2": 4}
+
+
+def fast_dequant(spec: ref.PackedSpec, scale_dtype: str | None = None, rows: np.ndarray | None = None) -> np.ndarray:
+    """float32 dequant of ``spec`` (or of the listed ``rows``) through the oracle's C restatement
+    (OpenMP, bit-exact with ``ref.dequant`` -- tests/test_oracle_c.py): the checker for
+    full-size matrices, where the numpy restatement would take minutes. ``scale_dtype`` is the
+    dtype the device sees ('e8m0', 'float16', 'bfloat16', 'float32' or None for the spec's own)."""
+    import ctypes
+
+    from oracle import build as obuild
+
+    global _CLIB
+    if _CLIB is None:
+        _CLIB = obuild.load()
+    n, k = spec.shape
+    sdt, sc = 0, None
+    if spec.scales is not None:
+        name = scale_dtype or spec.scale_dtype or ref.dtype_name(spec.scales.dtype)
+        if name == "e8m0":  # E8M0 bytes decode to exactly these float32 powers of two
+            name = "float32"
+        if name == "float16":
+            sdt, sc = 12, np.ascontiguousarray(spec.scales.astype(np.float16))
+        elif name == "bfloat16":
+            sdt, sc = 13, np.ascontiguousarray(spec.scales.astype(ref.BF16)).view(np.uint16)
+        else:
+            sdt, sc = 14, np.ascontiguousarray(spec.scales.astype(np.float32))
+    ptr = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    data = np.ascontiguousarray(spec.data)
+    bits = ref.FORMATS[spec.format][0]
+    if rows is None:
+        out = np.empty((n, k), np.float32)
+        rc = _CLIB.oref_dequant_f32(ptr(data), data.size, _C_FMT[spec.format], n, k,
+                                    None if sc is None else ptr(sc), sdt, spec.block_size, ptr(out))
+        assert rc == 0
+        return out
+    # selected rows: each row is byte-aligned when k * bits % 8 == 0 (all benchmark shapes)
+    assert (k * bits) % 8 == 0
+    rb, nblk = k * bits // 8, sc.shape[1] if sc is not None else 0
+    out = np.empty((len(rows), k), np.float32)
+    for i, r in enumerate(np.asarray(rows)):
+        d = np.ascontiguousarray(data[r * rb:(r + 1) * rb])
+        s = None if sc is None else np.ascontiguousarray(sc[r:r + 1])
+        o = out[i:i + 1]
+        rc = _CLIB.oref_dequant_f32(ptr(d), d.size, _C_FMT[spec.format], 1, k, None if s is None else ptr(s), sdt,
+                                    spec.block_size, ptr(o))
+        assert rc == 0 and nblk >= 0
+    return out

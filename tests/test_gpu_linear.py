@@ -1,8 +1,9 @@
 """Fused packed linear (GEMV / tcgen05 GEMM / SIMT) against the float32 oracle.
 
-Shapes cover the headline configs (c1 and c2 at full size; c3 at full K with fewer rows,
-plus a sampled-rows check at full size), odd tails, every format and scale dtype, and the
-three x / y dtypes. Tolerances: tests/helpers.py.
+Shapes cover the headline configs (c1 and c2 at full size; c3 at full K with fewer rows --
+the full-size c3 GEMM and the other shapes the benchmark times are in test_gpu_fullsize.py),
+odd tails, every format and scale dtype, and the three x / y dtypes. Tolerances:
+tests/helpers.py.
 """
 
 import functools
@@ -211,3 +212,28 @@ def test_gemm_rejects_inexact_group_scales(bs):
     assert linear_plan(w, torch.float16, 64, torch.float16, "gemm") is None
     assert linear_plan(w, torch.float16, 64, torch.float16, "auto") == "gemv"
     assert linear_plan(w, torch.float16, 65, torch.float16, "auto") == "simt"
+
+
+@pytest.mark.parametrize("m", [1, 8, 64])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_dtype_argument_and_cast_call_forms(m, dt):
+    """The two call forms of a low-precision output: ``matmul(W, x.T, dtype=dt)`` and
+    ``matmul(W, x.T).cast(dt)`` (the form the benchmark configs name: fp32 accumulate, 16-bit
+    output). The reference's ``dtype=`` also makes tinygrad accumulate in ``dt``
+    (codegen/linalg.py:173-174); here every fused kernel accumulates in fp32 and rounds once, so
+    both forms are checked against the fp32 oracle rounded to ``dt`` and agree to one ulp."""
+    import tinygrad_dx12_b200 as tg
+
+    spec = _spec("fp4_e2m1", 2048, 4096, 32, "e8m0", 9)
+    w = to_device(spec, DEV, "e8m0")
+    x = torch.randn((m, 4096), device=DEV).to(dt)
+    y_dtype = tg.matmul(w, x.t(), dtype=dt)
+    y_cast = tg.matmul(w, x.t()).to(dt)
+    assert y_dtype.dtype == dt and y_cast.dtype == dt and y_dtype.shape == (2048, m)
+    r = x.float().cpu().numpy() @ _wref(spec, "e8m0").T
+    name = "bfloat16" if dt == torch.bfloat16 else "float16"
+    assert_close(y_dtype.t().float().cpu().numpy(), r, name)
+    assert_close(y_cast.t().float().cpu().numpy(), r, name)
+    ulp = 2.0 ** (-8 if dt == torch.bfloat16 else -11)
+    diff = (y_dtype.float() - y_cast.float()).abs()
+    assert torch.all(diff <= ulp * y_cast.float().abs() * 2 + 1e-30)

@@ -724,8 +724,9 @@ int32_t launch_skinny(const LinearArgs &a, cudaStream_t stream) {
 // ---- allocation-free variant (b200_packed_linear_noalloc) ---------------------------------
 // The split-K scratch (row-block tickets, then fp32 partials) lives in one fixed device array
 // of this translation unit; nothing is allocated. The tickets must start at zero: the array is
-// zero-initialised when the module loads, setup clears them once more, and every reducing CTA
-// resets its ticket. Calls that overlap in time on one device share the array and race.
+// zero-initialised when the module loads and every reducing CTA resets its ticket, so set-up
+// writes nothing (a memset there would be unordered against a caller's non-blocking stream).
+// Calls that overlap in time on one device share the array and race.
 namespace b200 {
 namespace skinny {
 
@@ -736,7 +737,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH
 static std::mutex g_noalloc_mutex;
 static std::map<int, unsigned char *> g_noalloc_base;  // device -> address of the array
 
-// Resolve the array's device address once per device (and clear the tickets).
+// Resolve the array's device address once per device (with that device current).
 static int32_t noalloc_scratch(unsigned char *&base) {
   int dev = 0;
   B200_CUDA_TRY(cudaGetDevice(&dev));
@@ -748,7 +749,6 @@ static int32_t noalloc_scratch(unsigned char *&base) {
   }
   void *p = nullptr;
   B200_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-  B200_CUDA_TRY(cudaMemset(p, 0, NOALLOC_TICKETS * sizeof(unsigned int)));
   base = static_cast<unsigned char *>(p);
   g_noalloc_base[dev] = base;
   return B200_OK;
