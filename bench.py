@@ -436,7 +436,8 @@ def run_configs(args, device, world, rank):
                              "peak": "bf16_tflops_sustained (long loop)", "kernel": linear_plan(sh.gu, torch.bfloat16, m5,
                                                                                               torch.bfloat16),
                              "flops_per_layer": flops,
-                             "note": "weights of one layer stay in L2 between the 5 graph launches"}
+                             "note": "one layer's packed weights (454 MB) are larger than the 126 MB L2, so every "
+                                     "launch reads them from HBM; at 2048 tokens the layer is tensor-bound"}
     del layer, sh, ws5, xs, ys
 
     # c4 INT4 stack, one token through 32 layers on this GPU (no tensor parallelism)
@@ -633,6 +634,104 @@ def cpu_baseline(nthreads: int, budget_s: float) -> dict:
                       f"{sec * 1e3:.1f} ms/call; oracle/cpu_ref.c decode-to-fp32 row + fp32 dot, OpenMP"}
 
 
+def cpu_configs(nthreads: int, budget_s: float) -> dict:
+    """The reference's CPU path timed for every benchmark config on this host's cores, two ways:
+
+    * "port": oracle/cpu_ref.c (the C restatement: decode each weight row to fp32, fp32 dot
+      products; OpenMP over rows, `nthreads` threads);
+    * "numpy": the reference's CPU branch as written (codegen/linalg.py:169-174): decode the
+      packed matrix to a materialised fp32 tensor (the `.contiguous()` at :172) with the numpy
+      restatement, then x @ W^T through numpy's BLAS sgemm. Timed on the first 1024 weight rows
+      and scaled by rows / 1024 (decode and sgemm are both linear in the rows).
+
+    Samples are bounded so the whole leg takes a minute or two: c3 at M = 64 of its 4096 tokens,
+    one layer of the c4 / c5 stacks at M=1 (per-layer figures times the layer count). Values are
+    in each config's own metric (GB/s of algorithmic bytes for the decode shapes, TFLOP/s for c3).
+    """
+    from oracle import build as obuild
+    from oracle import packed_ref as ref
+
+    clib = obuild.load()
+    P = ctypes.c_void_p
+    fmt_code = {"int4": 0, "uint4": 1, "fp4_e2m1": 2, "fp6_e2m3": 3, "fp6_e3m2": 4}
+    out = {}
+    t_leg = time.perf_counter()
+
+    def timed(fn, reps_budget):
+        fn()  # warm-up
+        times, t0 = [], time.perf_counter()
+        while True:
+            a = time.perf_counter()
+            fn()
+            times.append(time.perf_counter() - a)
+            if time.perf_counter() - t0 >= reps_budget and len(times) >= 2:
+                break
+        return statistics.median(times), len(times)
+
+    def both(name, spec, m, xdt, per):
+        rng = np.random.default_rng(1)
+        x = rng.standard_normal((m, spec.shape[1])).astype(np.float32)
+        xs = x.astype(ref.BF16) if xdt == "bfloat16" else x.astype(np.float16)
+        sdt = 16 if spec.scale_dtype == "float32" else 12
+        sc = ref.e8m0_bytes(spec.scales) if sdt == 16 else spec.scales
+        y = np.empty((m, spec.shape[0]), np.float32)
+
+        def port():
+            rc = clib.oref_linear(spec.data.ctypes.data_as(P), spec.data.size, fmt_code[spec.format], spec.shape[0],
+                                  spec.shape[1], sc.ctypes.data_as(P), sdt, spec.block_size,
+                                  np.ascontiguousarray(xs).ctypes.data_as(P), 13 if xdt == "bfloat16" else 12, m,
+                                  y.ctypes.data_as(P), nthreads)
+            assert rc == 0
+
+        rows = min(1024, spec.shape[0])
+        rb = spec.shape[1] * ref.FORMATS[spec.format][0] // 8
+        part = ref.PackedSpec(spec.data[:rows * rb], spec.format, (rows, spec.shape[1]), spec.scales[:rows],
+                              spec.block_size, spec.scale_dtype)
+
+        def numpy_path():
+            ref.packed_linear_ref(part, xs.astype(np.float32))
+
+        tp, np_ = timed(port, budget_s / 24)
+        tn, nn = timed(numpy_path, budget_s / 48)
+        tn *= spec.shape[0] / rows
+        out[name] = {"port": per(tp), "numpy": per(tn), "port_s_per_call": round(tp, 4),
+                     "numpy_s_per_call": round(tn, 4), "calls": [np_, nn]}
+
+    gb = lambda nbytes: (lambda sec: round(nbytes / sec / 1e9, 3))  # noqa: E731
+    c1 = ref.make_packed(np.random.default_rng(0), "int4", 4096, 4096, 32, "f16u")
+    both("c1_int4_m1", c1, 1, "float16", gb(algo_bytes(dict(fmt="int4", n=4096, k=4096, block=32, scale="f16u", m=1))))
+    c2 = ref.make_packed(np.random.default_rng(0), "fp4_e2m1", 8192, 8192, 32, "e8m0")
+    for m in (1, 8, 32):
+        both(f"c2_fp4_m{m}", c2, m, "bfloat16", gb(algo_bytes(dict(GEMV_CFG, m=m))))
+    del c2
+    c3 = ref.make_packed(np.random.default_rng(0), "fp6_e3m2", 14336, 4096, 4096, "f16row")
+    m3 = 64
+    both("c3_fp6_gemm", c3, m3, "float16", lambda sec: round(2 * m3 * 14336 * 4096 / sec / 1e12, 5))
+    out["c3_fp6_gemm"]["sample"] = f"M={m3} of 4096 tokens (TFLOP/s of the sample; time is linear in M here)"
+    del c3
+    for name, cfg in (("c4_stack_m1", "C4"), ("c5_stack_m1", "C5")):
+        from tinygrad_dx12_b200 import stack as S
+        sc_ = getattr(S, cfg)
+        sh = sc_.proj_shapes()
+        layer_bytes = sc_.layer_weight_bytes()
+        tp = tn = 0.0
+        for proj, (n, k) in sh.items():
+            kind = "e8m0" if sc_.scale == "e8m0" else "f16u"
+            spec = ref.make_packed(np.random.default_rng(hash(proj) & 0xFFFF), sc_.fmt, n, k, sc_.block, kind)
+            both(f"_{name}_{proj}", spec, 1, "bfloat16" if sc_.scale == "e8m0" else "float16", lambda sec: sec)
+            tp += out[f"_{name}_{proj}"]["port_s_per_call"]
+            tn += out[f"_{name}_{proj}"]["numpy_s_per_call"]
+            del out[f"_{name}_{proj}"], spec
+        out[name] = {"port": round(layer_bytes / tp / 1e9, 3), "numpy": round(layer_bytes / tn / 1e9, 3),
+                     "port_ms_per_token": round(tp * sc_.layers * 1e3, 1),
+                     "numpy_ms_per_token": round(tn * sc_.layers * 1e3, 1),
+                     "sample": f"one layer's seven projections at M=1, times {sc_.layers} layers"}
+    out["unit"] = "GB/s of algorithmic bytes (c3: TFLOP/s)"
+    out["cores"] = nthreads
+    out["leg_s"] = round(time.perf_counter() - t_leg, 1)
+    return out
+
+
 def profile_case(case: str, launches: int):
     """Small untimed workload for ncu captures: `launches` plain b200_packed_linear calls.
 
@@ -717,6 +816,7 @@ def main():
     if rank == 0 and res is not None:
         if not args.no_cpu and world == 1:
             res["cpu_baseline"] = cpu_baseline(nthreads, args.cpu_budget)
+            res["cpu_configs"] = cpu_configs(nthreads, args.cpu_budget)
         print(json.dumps(res))
 
 

@@ -70,10 +70,13 @@ extern "C" {
 #define B200_DT_E8M0 16   /* decoded-by-definition power-of-two scale byte (2^(b-127)) */
 
 /* ---- matmul path selection (b200_packed_linear `path`) ----------------------------- */
-#define B200_PATH_AUTO 0    /* GEMV for m <= 32, tcgen05 GEMM above, generic otherwise */
-#define B200_PATH_GEMV 1    /* force the fused decode GEMV                              */
+#define B200_PATH_AUTO 0    /* the best kernel that takes the operands (below)          */
+#define B200_PATH_GEMV 1    /* force the mma.sync decode GEMV / few-token GEMM (m <= 64) */
 #define B200_PATH_GEMM 2    /* force the tcgen05 GEMM                                   */
 #define B200_PATH_SIMT 3    /* force the fp32 CUDA-core fused kernel                    */
+#define B200_PATH_MX 4      /* force the block-scaled tcgen05 decode kernel: FP4 / FP6
+                               weights (per-32 E8M0, per-row or no scales), bf16 x up to
+                               64 tokens or fp16 x up to 42, K % 256 == 0 */
 /* OR-able flag: launch with programmatic dependent launch (PDL). The kernel may start while
  * the previous kernel on the stream is still running; it streams its packed weights and
  * scales at once and waits for that kernel before it reads x or writes y. Only valid when

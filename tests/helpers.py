@@ -4,8 +4,14 @@ Parity bar (stated once, used by every linear test):
 * dequantised values: bitwise equality of the float32 (or other output dtype) patterns,
   including -0.0;
 * fused matmul outputs: with r the float32 oracle result cast to the output dtype,
-  ``max |y - r| / max(|r|, floor) <= 1e-2`` with ``floor = 1e-3 * rms(r)`` and
+  ``max |y - r| / max(|r|, floor) <= 1e-2`` with ``floor = 1e-2 * rms(r)`` and
   ``||y - r||_F / ||r||_F <= 1e-3``, all accumulation in float32.
+
+The floor: an elementwise relative error is ill-posed for outputs near zero, so outputs
+smaller than 1 % of the RMS output are held to an absolute bound of 1e-4 * rms(r), the scale
+of float32 accumulation error over thousands of terms on the tensor cores (their adds into the
+fp32 accumulator are not round-to-nearest). Failures report the worst element's |r| and
+|y - r| in units of rms(r).
 """
 
 from __future__ import annotations
@@ -15,7 +21,7 @@ import torch
 
 from oracle import packed_ref as ref
 
-ELEM_TOL, FRO_TOL, FLOOR = 1e-2, 1e-3, 1e-3
+ELEM_TOL, FRO_TOL, FLOOR = 1e-2, 1e-3, 1e-2
 
 TORCH_OF = {"float16": torch.float16, "bfloat16": torch.bfloat16, "float32": torch.float32, "float64": torch.float64}
 
@@ -66,10 +72,22 @@ def errors(y: np.ndarray, r: np.ndarray) -> tuple[float, float]:
     return elem, fro
 
 
+def worst(y: np.ndarray, r: np.ndarray) -> str:
+    """The element with the largest floored relative error, in units of rms(r)."""
+    y = y.astype(np.float64)
+    r = r.astype(np.float64)
+    rms = max(np.sqrt(np.mean(r * r)), 1e-30)
+    rel = np.abs(y - r) / np.maximum(np.abs(r), max(FLOOR * rms, 1e-30))
+    i = np.unravel_index(int(np.argmax(rel)), rel.shape)
+    return (f"worst at {tuple(int(v) for v in i)}: |r| = {abs(r[i]) / rms:.3e} rms, |y - r| = "
+            f"{abs(y[i] - r[i]) / rms:.3e} rms, {int(np.sum(rel > ELEM_TOL))} elements over {ELEM_TOL}")
+
+
 def assert_close(y: np.ndarray, r32: np.ndarray, out_dtype: str) -> tuple[float, float]:
     r = r32.astype(ref.np_dtype(out_dtype)).astype(np.float64) if out_dtype != "float32" else r32
     elem, fro = errors(y, r)
-    assert elem <= ELEM_TOL and fro <= FRO_TOL, f"elementwise {elem:.3e} (<= {ELEM_TOL}), frobenius {fro:.3e} (<= {FRO_TOL})"
+    assert elem <= ELEM_TOL and fro <= FRO_TOL, (
+        f"elementwise {elem:.3e} (<= {ELEM_TOL}), frobenius {fro:.3e} (<= {FRO_TOL}); {worst(y, r)}")
     return elem, fro
 
 

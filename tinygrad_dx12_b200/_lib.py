@@ -25,7 +25,7 @@ DT = {
     "uint64": 9, "fp8e4m3": 10, "fp8e5m2": 11, "float16": 12, "bfloat16": 13, "float32": 14, "float64": 15,
     "e8m0": 16,
 }
-PATH = {"auto": 0, "gemv": 1, "gemm": 2, "simt": 3}
+PATH = {"auto": 0, "gemv": 1, "gemm": 2, "simt": 3, "mx": 4}
 PATH_NAME = {v: k for k, v in PATH.items()}
 
 

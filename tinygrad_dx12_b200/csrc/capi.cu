@@ -132,11 +132,15 @@ static bool fill_linear(const b200_packed_desc *w, const void *x, int32_t x_dtyp
   return x_stride_k == 1;
 }
 
-static int32_t plan(const LinearArgs &a, bool kstride_ok, int32_t path) {
+// Kernel for these operands. `mx_ok` = false leaves the block-scaled decode kernel out (its
+// workspace cannot be allocated during a stream capture).
+static int32_t plan(const LinearArgs &a, bool kstride_ok, int32_t path, bool mx_ok = true) {
   if (!kstride_ok) return B200_ERR_UNSUPPORTED;
   path &= 0xFF;  // flag bits (B200_FLAG_*) do not select a kernel
   const bool tc = gemv_tc_supported(a) || skinny_supported(a), gm = gemm_supported(a), simt = simt_supported(a);
+  const bool mx = mx_ok && mx_supported(a);
   switch (path) {
+    case B200_PATH_MX: return mx ? B200_PATH_MX : B200_ERR_UNSUPPORTED;
     case B200_PATH_AUTO:
       if (a.m <= 32 && tc) return B200_PATH_GEMV;
       if (a.m > 32 && gm) return B200_PATH_GEMM;
@@ -169,9 +173,10 @@ int32_t b200_packed_linear(const b200_packed_desc *w, const void *x, int32_t x_d
   LinearArgs a;
   const bool ks = fill_linear(w, x, x_dtype, m, x_stride_m, x_stride_k, y, y_dtype, y_stride_m, y_stride_n, a);
   a.flags = path & ~0xFF;
-  const int32_t p = plan(a, ks, path);
   cudaStream_t s = (cudaStream_t)stream;
+  const int32_t p = plan(a, ks, path, mx_ready(s));
   switch (p) {
+    case B200_PATH_MX: return launch_mx(a, s);
     case B200_PATH_GEMV:
       if (a.m > 2) return launch_skinny(a, s);
       return gemv_stream_supported(a) ? launch_gemv_stream(a, s) : launch_gemv_tc(a, s);
@@ -291,11 +296,14 @@ int32_t b200_device_status(int32_t device, uint32_t *flags, int32_t clear) {
   unsigned int v = 0, u = 0;
   if (int32_t rc = gemm_device_error(&v, clear != 0)) return rc;
   if (int32_t rc = gemv_device_error(&u, clear != 0)) return rc;
-  unsigned int w = 0, z = 0, dd = 0;
+  unsigned int w = 0, z = 0, dd = 0, mxe = 0;
   if (int32_t rc = skinny_device_error(&w, clear != 0)) return rc;
   if (int32_t rc = stackops_device_error(&z, clear != 0)) return rc;
   if (int32_t rc = gemm_dense_device_error(&dd, clear != 0)) return rc;
-  *flags = v | u | w | z | dd;
+  if (int32_t rc = mx_device_error(&mxe, clear != 0)) return rc;
+  *flags = v | u | w | z | dd | mxe;
+  if (clear != 0 && *flags != 0)  // a kernel gave up mid-way: its split-tile tickets may be half counted
+    if (int32_t rc = mx_reset_tickets()) return rc;
   return B200_OK;
 }
 
@@ -312,11 +320,12 @@ int32_t b200_packed_linear_multi(const b200_packed_desc *w, const void *x, int32
   LinearArgs a;
   const bool ks = fill_linear(w, x, x_dtype, m, x_stride_m, 1, y[0], y_dtype, y_stride_m, 1, a);
   a.flags = flags & ~0xFF;
-  const int32_t p = plan(a, ks, B200_PATH_AUTO);
   cudaStream_t s = (cudaStream_t)stream;
-  if (p == B200_PATH_GEMV && a.m <= 2) {  // the decode GEMV epilogue writes every destination
+  const int32_t p = plan(a, ks, B200_PATH_AUTO, mx_ready(s));
+  if (p == B200_PATH_MX || (p == B200_PATH_GEMV && a.m <= 2)) {  // these epilogues write every destination
     a.ncopy = n_y - 1;
     for (int i = 1; i < n_y; ++i) a.ycopy[i - 1] = y[i];
+    if (p == B200_PATH_MX) return launch_mx(a, s);
     return gemv_stream_supported(a) ? launch_gemv_stream(a, s) : launch_gemv_tc(a, s);
   }
   int32_t rc = B200_ERR_UNSUPPORTED;

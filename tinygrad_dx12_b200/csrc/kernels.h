@@ -59,6 +59,14 @@ int32_t skinny_device_error(unsigned int *v, bool clear);
 // same kernel, split-K scratch from a fixed device array instead of a library workspace
 int32_t launch_skinny_noalloc(const LinearArgs &a, cudaStream_t stream);
 
+// block-scaled tcgen05 decode kernel (kind::mxf8f6f4) for FP4 / FP6 weights and 1..64 tokens
+// (gemv_mx.cu): the packed codes are the MMA's A operand, x is split into exact E4M3 pieces
+bool mx_supported(const LinearArgs &a);
+bool mx_ready(cudaStream_t stream);  // its workspace exists or can be allocated now
+int32_t launch_mx(const LinearArgs &a, cudaStream_t stream);
+int32_t mx_device_error(unsigned int *v, bool clear);
+int32_t mx_reset_tickets();  // after a device error: zero the split-tile tickets on this device
+
 // dense fp16 / bf16 tcgen05 GEMM for ordinary matmuls (gemm_dense.cu): c = a @ b with a
 // row-major (k contiguous) and b K-major (k contiguous per column), fp32 accumulation
 bool gemm_dense_supported(const void *a, int adt, int64_t sam, int64_t sak, const void *b, int bdt, int64_t sbk,

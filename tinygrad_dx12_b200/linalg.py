@@ -30,7 +30,7 @@ from .packed import PackedTensor, matrix_intermediate, stream_ptr, ctypes_ref
 
 SCOPES = ("auto", "Wave", "ThreadGroup", "tiled")
 FUSED_IO = (torch.float16, torch.bfloat16, torch.float32)
-_SCOPE_PATHS = {"auto": ("auto",), "Wave": ("gemv", "simt"), "ThreadGroup": ("gemm",)}
+_SCOPE_PATHS = {"auto": ("auto",), "Wave": ("mx", "gemv", "simt"), "ThreadGroup": ("gemm",)}
 
 
 def _device_of(op) -> torch.device:
@@ -135,7 +135,7 @@ def _packed_linear_multi(w: PackedTensor, x: torch.Tensor, y_ptrs, out_dtype: to
 
 
 def linear_plan(w: PackedTensor, x_dtype: torch.dtype, m: int, out_dtype: torch.dtype, path: str = "auto") -> str | None:
-    """Name of the fused kernel the library would run ('gemv', 'gemm', 'simt') or None."""
+    """Name of the fused kernel the library would run ('mx', 'gemv', 'gemm', 'simt') or None."""
     d = w.desc()
     rc = _lib.lib().b200_packed_linear_plan(ctypes_ref(d), _lib.DT[D.name(x_dtype)], m, _lib.DT[D.name(out_dtype)],
                                             _lib.PATH[path])
@@ -151,7 +151,7 @@ def choose_matrix(w: PackedTensor, x_dtype: torch.dtype, m: int, out_dtype: torc
     for path in _SCOPE_PATHS[scope]:
         plan = linear_plan(w, x_dtype, m, out_dtype, path)
         if plan is not None:
-            return ({"gemv": "Wave", "gemm": "ThreadGroup", "simt": "Wave"}[plan], plan)
+            return ({"mx": "Wave", "gemv": "Wave", "gemm": "ThreadGroup", "simt": "Wave"}[plan], plan)
     return ("tiled", None)
 
 

@@ -44,13 +44,14 @@ def stream_ptr(device: torch.device) -> int:
 
 @dataclass(frozen=True)
 class PackedTensor:
-    """A contiguous low-bit tensor stored least-significant payload first in bytes.
+    """Packed low-bit weights on a CUDA device, in the byte layout of tinygrad-dx12.
 
-    ``shape`` gives the logical elements and ``data`` is a flat uint8 tensor. Six-bit
-    elements may straddle bytes. FP4 and FP6 use finite OCP payloads. Optional numeric
-    ``scales`` have shape ``shape[:-1] + (ceil(K/block_size),)``; each scale applies to
-    one block along the final dimension. A ``torch.float8_e8m0fnu`` scale tensor is read
-    as the power of two it encodes.
+    ``data`` is a 1-D uint8 tensor holding the codes of a tensor of logical shape ``shape``
+    back to back, lowest bits first (a 6-bit code can span two bytes). ``format`` names the
+    code type (``FORMATS``: int4, uint4, and the OCP FP4 E2M1 / FP6 E2M3 / FP6 E3M2 codes,
+    all finite). ``scales``, when given, holds one multiplier per run of ``block_size`` codes
+    along the last axis, shape ``shape[:-1] + (ceil(K / block_size),)``, on the same device;
+    a ``torch.float8_e8m0fnu`` tensor counts as the powers of two its bytes encode.
     """
 
     data: torch.Tensor
@@ -131,11 +132,11 @@ class PackedTensor:
         return torch.int32 if integer else torch.float32
 
     def unpack(self, dtype: torch.dtype | None = None) -> torch.Tensor:
-        """Decode to numeric elements and apply scales at their original K boundaries.
+        """The decoded tensor (codes times their block's scale) as ``dtype``, via ``b200_dequant``.
 
-        Floating payloads and scaled integers default to float32 (float64 with float64
-        scales); unscaled integers default to int32. Unscaled, exactly representable FP8
-        destinations use the direct encoding of dx12.py:78-92. Runs ``b200_dequant``.
+        Without ``dtype``: float32 for FP codes and for scaled integers (float64 when the scales
+        are float64), int32 for unscaled integers. FP codes without scales requested as an FP8
+        type that holds them exactly are re-encoded bit for bit (dx12.py:78-92).
         """
         dtype = dtype or self.default_dtype()
         _require_cuda(self.data, "packed data")
@@ -188,10 +189,11 @@ def _intermediate_for(ka, kb) -> torch.dtype:
 
 
 def matrix_intermediate(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor, native16: bool = False) -> torch.dtype:
-    """Shared dtype promotion after selecting an exact packed storage representation (dx12.py:115-138).
+    """The dtype both operands of a matmul are brought to (dx12.py:115-138).
 
-    Prefer a common FP8 encoding when both operands fit; otherwise promote the declared
-    types. ``native16`` is accepted for signature compatibility and changes nothing.
+    An FP8 type is chosen when it holds both operands exactly (unscaled FP4/FP6 codes or FP8
+    tensors); otherwise the declared types are promoted, a scaled packed operand counting as
+    at least float32. ``native16`` exists so reference call sites keep working; it is ignored.
     """
     return _intermediate_for(_operand_key(a), _operand_key(b))
 
