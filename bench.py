@@ -285,6 +285,9 @@ def run_gpu_arm(args, world, rank, local):
     configs = None
     if not args.no_configs:
         configs = run_configs(args, device, world, rank)
+    strong = None
+    if not args.no_configs:
+        strong = run_strong(args, device, world, rank)
     peaks = measured_peaks()
     result = None
     if rank == 0:
@@ -329,6 +332,8 @@ def run_gpu_arm(args, world, rank, local):
             result["stack"] = stack
         if configs is not None:
             result["configs"] = configs
+        if strong is not None:
+            result["strong_scaling"] = strong
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -459,6 +464,73 @@ def run_configs(args, device, world, rank):
                                   "kernel": linear_plan(st.layers[0].gu, S.C4.act, m4, S.C4.act),
                                   "note": "INT4 group-128 fp16 scales; one GPU, whole stack as one CUDA graph"}
     del st
+    return out
+
+
+def run_strong(args, device, world, rank):
+    """Strong scaling of the single-matrix configs (c1, c2 at M=1, c3 at M=4096): the one matrix
+    is split column-parallel over the ranks (each rank owns N / world output rows of the same
+    weights, x replicated; no collective: each rank's rows are independent outputs). Time = max
+    over ranks; value = the whole matrix's algorithmic bytes (or flops) / that time."""
+    import torch
+    import torch.distributed as dist
+    from tinygrad_dx12_b200 import _lib
+    from tinygrad_dx12_b200.linalg import linear_plan
+
+    fn = _lib.lib().b200_packed_linear
+    peaks = measured_peaks()
+    out = {}
+
+    def max_ms(ms):
+        t = torch.tensor([ms], device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for name, base in (("c1_int4_m1", dict(fmt="int4", n=4096, k=4096, block=32, scale="f16u", xdt="float16", m=1)),
+                       ("c2_fp4_m1", dict(GEMV_CFG))):
+        cfg = dict(base, n=base["n"] // world)
+        per_copy = cfg["n"] * cfg["k"] // 2
+        copies = max(4, -(-4 * L2_BYTES // per_copy))
+        ws = make_weights(cfg, device, copies, seed=21 + rank)
+        xdt = getattr(torch, cfg["xdt"])
+        x = torch.randn((1, cfg["k"]), device=device).to(xdt)
+        y = torch.empty((1, cfg["n"]), device=device, dtype=xdt)
+        descs = [w.desc() for w in ws]
+        code = _lib.DT[cfg["xdt"]]
+
+        def launch(i, stream):
+            rc = fn(ctypes.byref(descs[i % copies]), x.data_ptr(), code, 1, cfg["k"], 1, y.data_ptr(), code, cfg["n"], 1,
+                    0x100, stream)
+            if rc:
+                raise RuntimeError(_lib.last_error())
+
+        ms = max_ms(_graph_time_ms(launch, max(20, min(args.steps, 100)), device))
+        total = algo_bytes(base)
+        gbs = total / (ms / 1e3) / 1e9
+        out[name] = {"rows_per_rank": cfg["n"], "us_per_call": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
+                     "per_gpu_frac_of_hbm": round(gbs / world / peaks["hbm_gbs"], 4),
+                     "kernel": linear_plan(ws[0], xdt, 1, xdt), "l2": f"{copies} rotating weight copies per rank"}
+        del ws
+    cfg = dict(GEMM_CFG, n=GEMM_CFG["n"] // world)
+    w = make_weights(cfg, device, 1, seed=31 + rank)[0]
+    x = (torch.randn((cfg["m"], cfg["k"]), device=device) / 8).to(torch.float16)
+    y = torch.empty((cfg["m"], cfg["n"]), device=device, dtype=torch.float16)
+    d = w.desc()
+    f16 = _lib.DT["float16"]
+
+    def launch_g(i, stream):
+        rc = fn(ctypes.byref(d), x.data_ptr(), f16, cfg["m"], cfg["k"], 1, y.data_ptr(), f16, cfg["n"], 1, 0, stream)
+        if rc:
+            raise RuntimeError(_lib.last_error())
+
+    ms = max_ms(_graph_time_ms(launch_g, 5, device))
+    tf = algo_flops(GEMM_CFG) / (ms / 1e3) / 1e12
+    out["c3_fp6_gemm"] = {"rows_per_rank": cfg["n"], "ms_per_call": round(ms, 4), "TFLOP/s": round(tf, 1),
+                          "per_gpu_frac_of_tensor_peak": round(tf / world / peaks["bf16_tflops_sustained"], 4),
+                          "kernel": linear_plan(w, torch.float16, cfg["m"], torch.float16),
+                          "l2": "weights larger than L2 at every split (44 MB / world + 34 MB of x)"}
+    out["parallelism"] = f"column-parallel N/{world} of one matrix, x replicated, no collective"
     return out
 
 

@@ -179,7 +179,8 @@ int32_t b200_device_status(int32_t device, uint32_t *flags, int32_t clear);
 int32_t b200_device_wait_flag(const int32_t *flag, int32_t expect, int64_t max_spins, int32_t *status,
                               void *stream);
 
-/* b200_packed_linear (path AUTO, unit k / n strides) writing the same result to n_y <= 8
+/* b200_packed_linear (unit k / n strides; `flags` = a B200_PATH_* in the low byte, AUTO = 0,
+ * OR-ed with B200_FLAG_* bits) writing the same result to n_y <= 8
  * destinations of one layout -- e.g. this rank's slot in every rank's peer-mapped buffer, the
  * push half of the tensor-parallel reduction. The decode GEMV (m <= 2) stores every destination
  * from its epilogue; other kernels compute into y[0] and copy. No counterpart in the reference. */

@@ -8,7 +8,8 @@
 * the streamed decode GEMV with far more 32-row blocks than resident CTAs: the c5 gate|up
   projection (57344 x 8192 FP4 E8M0, 1792 row blocks) and the c4 gate|up projection
   (28672 x 4096 INT4, fp16 group-128 scales, 896 row blocks), M = 1 and 2, all rows.
-* one full-size c4 layer and one full-size c5 layer through TPStack against the oracle chain.
+* one full-size c4 layer and one full-size c5 layer through TPStack: every projection against
+  the oracle on the input the chain fed it, and the chain's output against the oracle chain.
 
 The checker is the oracle: weights decoded by its C restatement (bit-exact with the numpy one,
 tests/test_oracle_c.py), products in float32 on the host. Tolerances are the parity bar of
@@ -108,8 +109,17 @@ def _c_linear(spec, x):
 @pytest.mark.parametrize("name,m", [("c4", 1), ("c4", 16), ("c5", 1)])
 def test_full_size_layer(name, m):
     """One full-size layer of the c4 (8B-shaped INT4) or c5 (70B-shaped FP4) stack through the
-    CUDA library (fused projections, glue kernels) against the oracle chain."""
-    from tests.stack_helpers import ACT, initial_h
+    CUDA library (fused projections, glue kernels).
+
+    Every projection is checked against the oracle on the activation the GPU chain fed it, with
+    the parity bar of tests/helpers.py. The chain's final h is then compared with the oracle
+    chain run from the same h0: the chain rounds to the activation dtype after every step, so a
+    one-ulp difference in an early rounding (fp32 sums in another order) moves later steps'
+    inputs; with bf16 activations (2^-8 relative per ulp) that spread reaches about 1e-3 of h
+    after one layer, so the end-to-end bound is 4e-3 (bf16) / 1e-3 (fp16) in relative
+    Frobenius norm."""
+    from tests.helpers import assert_close
+    from tests.stack_helpers import ACT, initial_h, spec_of
     from tinygrad_dx12_b200 import stack as S
 
     cfg = {"c4": S.C4, "c5": S.C5}[name]
@@ -120,12 +130,28 @@ def test_full_size_layer(name, m):
         w = S.make_matrix(cfg, layer, proj, "cpu")
         return PackedTensor(w.data.to(DEV), w.format, w.shape, w.scales.to(DEV), w.block_size)
 
-    st = S.TPStack(cfg, 0, 1, device=DEV, layers=1, matrix_fn=on_device)
+    class Recording(S.CudaOps):
+        def __init__(self):
+            super().__init__()
+            self.calls = []
+
+        def linear(self, w, x, out_dtype):
+            y = super().linear(w, x, out_dtype)
+            self.calls.append((w, x.clone(), y.clone()))
+            return y
+
+    ops = Recording()
+    st = S.TPStack(cfg, 0, 1, device=DEV, layers=1, matrix_fn=on_device, ops=ops)
     h = st.forward(initial_h(cfg, m).to(DEV))
     torch.cuda.synchronize()
+    assert len(ops.calls) == 4  # qkv, o, gate|up, down
+    act = ACT[cfg.act]
+    for w, x, y in ops.calls:
+        r = x.float().cpu().numpy() @ fast_dequant(spec_of(w)).T
+        assert_close(y.float().cpu().numpy(), r, act if y.dtype == cfg.act else "float32")
     y = h.float().cpu().numpy()
-    del st
-    r = stack_ref.stack_forward(_LazyLayers(cfg, 1), initial_h(cfg, m).float().numpy(), ACT[cfg.act], _c_linear)
+    del st, ops
+    r = stack_ref.stack_forward(_LazyLayers(cfg, 1), initial_h(cfg, m).float().numpy(), act, _c_linear)
     elem, fro = errors(y, r)
     assert np.all(np.isfinite(y))
-    assert elem <= 1e-2 and fro <= 1e-3, f"elementwise {elem:.3e}, frobenius {fro:.3e}"
+    assert fro <= (4e-3 if cfg.act == torch.bfloat16 else 1e-3), f"frobenius {fro:.3e} (elementwise {elem:.3e})"

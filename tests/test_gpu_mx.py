@@ -49,7 +49,7 @@ def _run(spec, sdt, m, xdt, ydt, seed=0, xscale=1.0, flags=0):
 
 @pytest.mark.parametrize("m", [1, 2, 3, 8, 16, 32, 33, 64])
 def test_c2_fp4_e8m0(m):
-    """Config c2 (FP4 E2M1 8192 x 8192, per-32 E8M0, bf16 x / y): 64 tiles x 64 stages over 148
+    """Config c2 (FP4 E2M1 8192 x 8192, per-32 E8M0, bf16 x / y): 64 tiles x 32 stages over 148
     CTAs, so every tile is shared by two or three CTAs."""
     _run(_spec("fp4_e2m1", 8192, 8192, 32, "e8m0", 2), "e8m0", m, "bfloat16", "bfloat16")
 
@@ -63,11 +63,13 @@ def test_formats_scales_x_dtypes(fmt, kind, sdt, xdt, m):
     _run(spec, sdt, m, xdt, "float32", xscale=0.25)
 
 
-@pytest.mark.parametrize("rows,cols", [(128, 512), (129, 768), (256, 8192), (4768, 1024), (57344, 8192)])
+@pytest.mark.parametrize("rows,cols", [(128, 512), (129, 512), (300, 1536), (256, 8192), (4768, 1024),
+                                       (57344, 8192)])
 @pytest.mark.parametrize("m", [1, 4])
 def test_stream_k_splits(rows, cols, m):
-    """Ragged rows, few stages, tiles shared by dozens of CTAs (256 x 8192: 128 units for 148
-    SMs, one unit each) and the c5 gate|up shape (448 tiles x 64 stages)."""
+    """Ragged rows, few stages, tiles shared by dozens of CTAs (256 x 8192: 64 units for 148
+    SMs, one unit each) and the c5 gate|up shape (448 tiles x 32 stages). Per-32 E8M0 scales
+    need K % 512 == 0 here (a 16-byte row of scale bytes per TMA box)."""
     _run(_spec("fp4_e2m1", rows, cols, 32, "e8m0", 4), "e8m0", m, "bfloat16", "bfloat16")
 
 
@@ -122,7 +124,7 @@ def test_multi_destination_epilogue():
     x = torch.randn((1, 4096), device=DEV).to(torch.bfloat16)
     outs = [torch.full((1, 1024), float("nan"), device=DEV) for _ in range(3)]
     ptrs = (ctypes.c_void_p * 3)(*[o.data_ptr() for o in outs])
-    _packed_linear_multi(w, x, ptrs, torch.float32, 1024)
+    _packed_linear_multi(w, x, ptrs, torch.float32, 1024, flags=4)  # B200_PATH_MX
     expect = _packed_linear(w, x, torch.float32, "mx")
     torch.cuda.synchronize()
     for o in outs:

@@ -321,7 +321,7 @@ int32_t b200_packed_linear_multi(const b200_packed_desc *w, const void *x, int32
   const bool ks = fill_linear(w, x, x_dtype, m, x_stride_m, 1, y[0], y_dtype, y_stride_m, 1, a);
   a.flags = flags & ~0xFF;
   cudaStream_t s = (cudaStream_t)stream;
-  const int32_t p = plan(a, ks, B200_PATH_AUTO, mx_ready(s));
+  const int32_t p = plan(a, ks, flags, mx_ready(s));  // the low byte selects a path, as in b200_packed_linear
   if (p == B200_PATH_MX || (p == B200_PATH_GEMV && a.m <= 2)) {  // these epilogues write every destination
     a.ncopy = n_y - 1;
     for (int i = 1; i < n_y; ++i) a.ycopy[i - 1] = y[i];

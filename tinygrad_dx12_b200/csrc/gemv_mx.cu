@@ -25,25 +25,22 @@
 // the last contributor (acquire-release ticket), which adds the fp32 partials of its tile in
 // CTA order (deterministic) and stores y.
 //
-// Roles (448 threads): warps 0-3 issue the TMA loads of a shared-memory ring (per stage two
-// boxes of weight codes through the 16U4/16U6 "align 16B" tensor-map types, which lay each
-// 16-code group into the 16-byte slot the MMA reads, and the stage's E8M0 weight scales). A
-// thread's TMA issues are serialised at several hundred cycles per box, so four threads issue
-// alternate stages of 16 KB of codes. Warps 10-13 split the stage's x into pieces straight into
-// the ring's B tiles and their scale atoms; warp 9 rearranges the weight scales into the
-// tensor-memory scale-factor layout (row r -> lane r % 32, column r / 32, byte = K block);
-// warp 8 lane 0 copies both scale atoms into tensor memory (tcgen05.cp, four rotating column
-// sets) and issues eight K=32 MMAs per stage into one of two fp32 accumulators; warps 4-7 read
-// the accumulators (tcgen05.ld) and finish the rows.
+// Roles (672 threads): warps 0-3 issue the TMA loads of a shared-memory ring (per stage the
+// weight codes -- one 128-byte box of packed FP4 for kind::mxf4, else two boxes through the
+// 16U4/16U6 "align 16B" tensor-map types, which lay each 16-code group into the 16-byte slot the
+// MMA reads -- and the stage's E8M0 weight scales); a thread's TMA issues are serialised at
+// several hundred cycles per box, so up to four threads issue alternate stages. Warps 17-20
+// split the stage's x into pieces straight into the ring's B tiles and their scale bytes. Warps
+// 8-15 (two sets of four, one tensor-memory lane quarter per warp; a set owns the ring slots of
+// one parity) write both scale-factor operands into tensor memory with tcgen05.st (row r ->
+// lane r % 32 in every quarter, column r / 32, byte = K block). Warp 16 lane 0 issues the MMAs
+// into one of two fp32 accumulators; warps 4-7 read the accumulators (tcgen05.ld) and finish
+// the rows.
 // Every wait is bounded (sm100.cuh); on give-up the kernel flags the device error word.
 #include <map>
 #include <mutex>
 
-#include "common.cuh"
-#include "kernels.h"
-#include "sm100.cuh"
-
-#include <cuda_fp4.h>
+#include "mx.cuh"
 
 namespace b200 {
 
@@ -54,9 +51,6 @@ int32_t mx_device_error(unsigned int *v, bool clear) {
 
 namespace mx {
 
-constexpr int TM = 128;           // weight rows per tile (the MMA's M)
-constexpr int KB = 128;           // K codes per tensor-map box of the packed types
-constexpr int KS = 2 * KB;        // K codes per stage
 // warps: 0-3 TMA producers, 4-7 epilogue, 8-15 scale-factor writers (two sets of four that take
 // alternate stages; in each, warp w writes tensor-memory lane quarter w % 4), 16 MMA issuer,
 // 17-20 x converters
@@ -64,16 +58,9 @@ constexpr int PROD_WARPS = 4, EPI_WARP0 = 4, SF_WARP0 = 8, MMA_WARP = 16, CONV_W
 constexpr int THREADS = 21 * 32;
 constexpr int MAX_STAGES = 8;
 constexpr int MAX_COLS = 128;     // m * pieces per call
-// tensor memory: two accumulators of up to 128 columns, then one scale-factor set of 16 columns
-// per ring slot (A box 0, A box 1, B box 0, B box 1: 4 columns each)
-constexpr uint32_t D_COL0 = 0, D_COL1 = 128, SF_COL = 256, TMEM_COLS = 512;
-enum { SM_E8M0 = 0, SM_ROW = 1, SM_NONE = 2 };
-
-// UMMA formats of the A operand (instruction descriptor bits 7..9)
-template <int FMT>
-__host__ __device__ constexpr uint32_t a_format() {
-  return FMT == B200_FMT_FP4_E2M1 ? 5u : FMT == B200_FMT_FP6_E2M3 ? 3u : 4u;
-}
+// tensor memory: two accumulators (columns [0, d1) and [d1, 2 d1)), then one scale-factor set of
+// 16 columns per ring slot (A box 0, A box 1, B box 0, B box 1: 4 columns each); the allocation
+// is the power of two that holds them, so small calls leave room for the next call's CTA on the SM
 
 struct Params {
   int64_t rows, cols;
@@ -82,10 +69,14 @@ struct Params {
   int grid;              // CTAs
   int m, P, N;           // tokens, pieces per token, MMA N
   int stages;            // ring depth
+  int nact;              // producers and converters in use: min(4, stages). An actor that owns
+                         // the stages i = a (mod nact) never gets more than one ring round ahead
+                         // of the consumers, so a slot's barrier phase parity is never ambiguous
   // per stage: codes [2][128 rows][128 B] at 0, x pieces [2][N rows][128 B] at b_off, raw
   // weight scales [128 rows][16 B] at sraw_off, x-piece scales [128 rows][8 K blocks] at xsf_off
   uint32_t stage_bytes, b_off, sraw_off, xsf_off;
   uint32_t tx;           // TMA transaction bytes per stage
+  uint32_t d1_col, sf_col, tmem_cols;  // tensor-memory layout
   uint32_t idesc;        // instruction descriptor without scale-factor ids
   const uint16_t *x;     // activations (bf16 or fp16), row stride ldx
   int64_t ldx;
@@ -99,165 +90,6 @@ struct Params {
   float *part;           // [grid][2][m][128] fp32 partials of split tiles
   unsigned int *tickets; // [ntiles]
 };
-
-__device__ __forceinline__ int64_t unit_start(const Params &p, int64_t c) { return c * p.units / p.grid; }
-
-// CTA whose unit range holds unit u.
-__device__ __forceinline__ int owner(const Params &p, int64_t u) {
-  int64_t c = u * p.grid / p.units;
-  while (c + 1 < p.grid && unit_start(p, c + 1) <= u) ++c;
-  while (c > 0 && unit_start(p, c) > u) --c;
-  return (int)c;
-}
-
-// D (+)= (A x SFA) * (B x SFB)^T, kind::mxf8f6f4, one E8M0 scale per 32 K per row of A and B.
-__device__ __forceinline__ void mma_mx(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc,
-                                       uint32_t sfa, uint32_t sfb) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, float (&v)[8]) {
-  uint32_t r[8];
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-// Split 8 activations (one lane's share of a 32-element block, 4 lanes per block) into P E4M3
-// pieces with the block's E8M0 scale; returns the scale byte. `v` holds the values as float.
-template <int P>
-__device__ __forceinline__ uint32_t split_pieces(float (&v)[8], uint2 (&out)[P]) {
-  float amax = 0.f;
-  uint32_t nonfinite = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float a = fabsf(v[i]);
-    nonfinite |= a <= 3.4e38f ? 0u : 1u;  // Inf or NaN
-    amax = fmaxf(amax, a);
-  }
-  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-  nonfinite |= __shfl_xor_sync(0xffffffffu, nonfinite, 1);
-  nonfinite |= __shfl_xor_sync(0xffffffffu, nonfinite, 2);
-  uint32_t byte;
-  if (nonfinite) byte = 255u;  // a NaN block scale: the block's products become NaN
-  else if (amax == 0.f) byte = 127u;
-  else {
-    const int b = ilogbf(amax) + 120;  // scale 2^(ilogb-7): the maximum lands in [128, 256)
-    byte = (uint32_t)(b < 1 ? 1 : b > 253 ? 253 : b);
-  }
-  const float inv = byte == 255u ? 0.f : __uint_as_float((254u - byte) << 23);  // 2^(127 - byte)
-#pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] *= inv;
-#pragma unroll
-  for (int q = 0; q < P; ++q) {
-    uint32_t w[4];
-#pragma unroll
-    for (int h = 0; h < 4; ++h) w[h] = __nv_cvt_float2_to_fp8x2(make_float2(v[2 * h], v[2 * h + 1]), __NV_SATFINITE, __NV_E4M3);
-    out[q] = make_uint2(w[0] | (w[1] << 16), w[2] | (w[3] << 16));
-    if (q + 1 < P) {
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const __half2_raw b2 = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)w[h], __NV_E4M3);
-        v[2 * h] -= __half2float(__ushort_as_half(b2.x));
-        v[2 * h + 1] -= __half2float(__ushort_as_half(b2.y));
-      }
-    }
-  }
-  return byte;
-}
-
-// Split 8 activations (one lane's share of a 32-element block, 4 lanes per block) into NP FP4
-// E2M1 pieces. Piece 0 takes the E8M0 block scale 2^e that puts the block maximum in [2, 4),
-// where the E2M1 grid step is 1, so its rounding error is at most 2^(e-1); piece q takes scale
-// 2^(e-2q), under which the remaining values stay within +-2 and round with an error of at most
-// a quarter step: every piece after the first adds two bits, and eight leave an error of at most
-// 2^(e-16), below 2^-17 of the block maximum. out[q] holds the 8 codes (low nibble = lower
-// element); the scale byte of piece q is byte0 - 2q.
-template <int NP>
-__device__ __forceinline__ uint32_t split_fp4(float (&r)[8], uint32_t (&out)[NP]) {
-  float amax = 0.f;
-  uint32_t nonfinite = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float a = fabsf(r[i]);
-    nonfinite |= a <= 3.4e38f ? 0u : 1u;  // Inf or NaN
-    amax = fmaxf(amax, a);
-  }
-  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-  nonfinite |= __shfl_xor_sync(0xffffffffu, nonfinite, 1);
-  nonfinite |= __shfl_xor_sync(0xffffffffu, nonfinite, 2);
-  if (nonfinite) {  // a NaN block scale on piece 0: the block's products become NaN
-#pragma unroll
-    for (int q = 0; q < NP; ++q) out[q] = 0u;
-    return 255u;
-  }
-  if (amax == 0.f) {
-#pragma unroll
-    for (int q = 0; q < NP; ++q) out[q] = 0u;
-    return 127u + 2u * (NP - 1);  // every piece's scale byte stays >= 127
-  }
-  const int b = ilogbf(amax) + 126;  // scale 2^(ilogb-1): the maximum lands in [2, 4)
-  const uint32_t byte = (uint32_t)(b < 2 * NP - 1 ? 2 * NP - 1 : b > 253 ? 253 : b);
-  float inv = __uint_as_float((254u - byte) << 23), scale = __uint_as_float(byte << 23);
-#pragma unroll
-  for (int q = 0; q < NP; ++q) {
-    uint32_t w = 0;
-#pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const __nv_fp4x2_storage_t c =
-          __nv_cvt_float2_to_fp4x2(make_float2(r[2 * h] * inv, r[2 * h + 1] * inv), __NV_E2M1, cudaRoundNearest);
-      w |= (uint32_t)c << (8 * h);
-      if (q + 1 < NP) {
-        const __half2_raw back = __nv_cvt_fp4x2_to_halfraw2(c, __NV_E2M1);
-        r[2 * h] -= __half2float(__ushort_as_half(back.x)) * scale;
-        r[2 * h + 1] -= __half2float(__ushort_as_half(back.y)) * scale;
-      }
-    }
-    out[q] = w;
-    inv *= 4.f;
-    scale *= 0.25f;
-  }
-  return byte;
-}
-
-// D (+)= (A x SFA) * (B x SFB)^T, kind::mxf4: E2M1 A and B, K = 64, one E8M0 scale per 32 K.
-__device__ __forceinline__ void mma_mxf4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc,
-                                         uint32_t sfa, uint32_t sfb) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
-      : "memory");
-}
-
-template <bool XBF16>
-__device__ __forceinline__ void load8(const uint16_t *src, float (&v)[8]) {
-  const uint4 raw = *reinterpret_cast<const uint4 *>(src);
-  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    if constexpr (XBF16) {
-      v[2 * i] = __uint_as_float(w[i] << 16);
-      v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-    } else {
-      v[2 * i] = __half2float(__ushort_as_half((unsigned short)(w[i] & 0xFFFFu)));
-      v[2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(w[i] >> 16)));
-    }
-  }
-}
 
 // P = 8: kind::mxf4 (FP4 weights, x in eight FP4 pieces, 256 packed codes per 128-byte row);
 // P = 2 or 3: kind::mxf8f6f4 (FP4 / FP6 weights, x in E4M3 pieces, two 128-code boxes per stage).
@@ -309,7 +141,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       *reinterpret_cast<uint4 *>(st + p.xsf_off + o) = make_uint4(0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
   }
   fence_proxy_async_smem();
-  if (warp == MMA_WARP) tmem_alloc(tmem_slot, TMEM_COLS);
+  if (warp == MMA_WARP) tmem_alloc(tmem_slot, p.tmem_cols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -324,7 +156,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       prefetch_tmap(&tmw);
       if constexpr (SMODE == SM_E8M0) prefetch_tmap(&tms);
       int64_t i = warp;
-      for (; i < n; i += PROD_WARPS) {
+      for (; i < n && warp < p.nact; i += p.nact) {
         const int slot = (int)(i % S);
         const uint32_t round = (uint32_t)(i / S);
         if (i >= S && !mbar_wait(&empty[slot], (round - 1u) & 1u, abort_flag)) break;
@@ -341,7 +173,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if constexpr (SMODE == SM_E8M0) tma_load_2d(st + p.sraw_off, &tms, (s * 8) & ~15, t * TM, &full[slot]);
       }
       if (*abort_flag) {  // let this thread's copies in flight land before the CTA exits
-        for (int64_t q = warp; q < (i < n ? i : n); q += PROD_WARPS)
+        for (int64_t q = warp; q < (i < n ? i : n); q += p.nact)
           if (q + S >= i) mbar_wait(&full[q % S], (uint32_t)((q / S) & 1), abort_flag, 200000000ull);
       }
     }
@@ -350,7 +182,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // converter warp cw takes the stages i = cw (mod 4) for every token
     const int cw = warp - CONV_WARP0;
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
-    for (int64_t i = cw; i < n; i += CONV_WARPS) {
+    for (int64_t i = cw; i < n && cw < p.nact; i += p.nact) {
       const int slot = (int)(i % S);
       const uint32_t round = (uint32_t)(i / S);
       if (i >= S && !mbar_wait(&empty[slot], (round - 1u) & 1u, abort_flag)) break;
@@ -406,7 +238,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == MMA_WARP) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t d_col[2] = {D_COL0, D_COL1};
+      const uint32_t d_col[2] = {0u, p.d1_col};
       int slot = 0;
       uint32_t round = 0;
       int seg = -1;
@@ -425,7 +257,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         const uint8_t *st = ring + (size_t)slot * p.stage_bytes;
         const uint32_t dcol = tmem + d_col[seg & 1];
-        const uint32_t sf = tmem + SF_COL + 16u * (uint32_t)slot;
+        const uint32_t sf = tmem + p.sf_col + 16u * (uint32_t)slot;
         if constexpr (MXF4) {
           const uint64_t ad = sw128_kmajor_desc(st), bd = sw128_kmajor_desc(st + p.b_off);
 #pragma unroll
@@ -459,11 +291,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     // Row r of a 128-row operand has its E8M0 scale of K block b at lane r % 32 (in every lane
     // quarter), column 4 * box + r / 32 of the slot's set, byte b: thread i0 of each of these
     // warps writes the words of rows i0, i0 + 32, i0 + 64, i0 + 96 into its own quarter.
+    // The set of a stage is its ring slot's parity: a set that owns a slot has waited on the
+    // slot's previous phase itself, so its next wait on that slot is never a phase ahead of it
+    // (stages split by index parity would not be, with an odd ring depth).
     const uint32_t quarter = (uint32_t)(warp & 3);
-    const int set = (warp - SF_WARP0) >> 2;  // this set writes the stages i = set (mod 2)
-    for (int64_t i = set; i < n; i += 2) {
-      const int slot = (int)(i % S);
-      const uint32_t round = (uint32_t)(i / S);
+    const int set = (warp - SF_WARP0) >> 2;
+    int slot = 0;
+    uint32_t round = 0;
+    for (int64_t i = 0; i < n; ++i, (++slot == S ? (slot = 0, ++round) : 0u)) {
+      if ((slot & 1) != set) continue;
       bool ok = mbar_wait(&bready[slot], round & 1u, abort_flag);
       if (SMODE == SM_E8M0) ok = ok && mbar_wait(&full[slot], round & 1u, abort_flag);
       if (!ok) break;
@@ -478,7 +314,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint2 bx = *reinterpret_cast<const uint2 *>(st + p.xsf_off + r * 8);
         w[q] = a.x, w[4 + q] = a.y, w[8 + q] = bx.x, w[12 + q] = bx.y;
       }
-      tmem_st_32x32b_x16(tmem + ((32u * quarter) << 16) + SF_COL + 16u * (uint32_t)slot, w);
+      tmem_st_32x32b_x16(tmem + ((32u * quarter) << 16) + p.sf_col + 16u * (uint32_t)slot, w);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -488,7 +324,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- epilogue: rows of the tile, one per thread ----------------
     const int r = (warp - EPI_WARP0) * 32 + lane;  // row within the tile = tensor-memory lane
     const uint32_t lane_base = (uint32_t)((warp - EPI_WARP0) * 32) << 16;
-    const uint32_t d_col[2] = {D_COL0, D_COL1};
+    const uint32_t d_col[2] = {0u, p.d1_col};
+    constexpr int TOK = P == 8 ? 1 : 8;  // tokens per accumulator read: TOK * P / 8 loads of 8 columns
     bool waited = false;
     int seg = 0;
     for (int64_t i = 0; i < n;) {
@@ -510,20 +347,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (row < p.rows) rs = load_as_f32(p.rscale, row, p.sdt);
       const int e = (u0 / p.nst == t) ? 0 : 1;  // this CTA's first or last tile
       float *mypart = p.part + ((size_t)blockIdx.x * 2 + e) * p.m * TM;
-      // tokens in chunks of 8: P * 8 accumulator columns each
-      for (int m0 = 0; m0 < p.m; m0 += 8) {
-        float acc[8];
+      // TOK tokens at a time: P * TOK accumulator columns
+      for (int m0 = 0; m0 < p.m; m0 += TOK) {
+        float acc[TOK];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+        for (int q = 0; q < TOK; ++q) acc[q] = 0.f;
 #pragma unroll
-        for (int c = 0; c < P; ++c) {
+        for (int c = 0; c < P * TOK / 8; ++c) {
           float v[8];
           tmem_ld_x8(tmem + lane_base + d_col[buf] + (uint32_t)(m0 * P + 8 * c), v);
 #pragma unroll
           for (int q = 0; q < 8; ++q) acc[(8 * c + q) / P] += v[q];  // column m0*P + 8c + q: token (8c+q)/P
         }
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < TOK; ++q) {
           const int mm = m0 + q;
           if (mm >= p.m) break;
           if (whole) {
@@ -587,21 +424,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == MMA_WARP) tmem_dealloc(tmem, TMEM_COLS);
+  if (warp == MMA_WARP) tmem_dealloc(tmem, p.tmem_cols);
 }
 
 // ---- per-(device, stream) workspace: fp32 partials of shared tiles and their tickets ----------
-struct Workspace {
-  float *part = nullptr;
-  unsigned int *tickets = nullptr;
-  size_t part_bytes = 0, tickets_n = 0;
-};
-constexpr size_t TICKETS = 16384;  // 128-row tiles: N <= 2M rows
 
 static std::mutex g_ws_mutex;
 static std::map<std::pair<int, cudaStream_t>, Workspace> g_ws;
 
-static int32_t workspace_for(cudaStream_t stream, bool may_allocate, Workspace *&out) {
+int32_t workspace_for(cudaStream_t stream, bool may_allocate, Workspace *&out) {
   int dev = 0;
   B200_CUDA_TRY(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lock(g_ws_mutex);
@@ -630,11 +461,6 @@ static int32_t workspace_for(cudaStream_t stream, bool may_allocate, Workspace *
 
 static int pieces_of(int xdt) { return xdt == B200_DT_BF16 ? 2 : 3; }
 
-static int scale_mode(const LinearArgs &a) {
-  if (a.scales == nullptr) return SM_NONE;
-  if (a.nblk == 1) return SM_ROW;
-  return SM_E8M0;
-}
 
 static size_t smem_for(const Params &p) { return 1024 + (size_t)p.stages * p.stage_bytes + 8 * (4 * p.stages + 5) + 16; }
 
@@ -661,11 +487,26 @@ static int32_t launch_t(const LinearArgs &a, const Workspace &w, cudaStream_t st
   p.sraw_off = p.b_off + (nbox * bbox + 1023) / 1024 * 1024;
   p.xsf_off = p.sraw_off + TM * 16;
   p.stage_bytes = (p.xsf_off + TM * 8 + 1023) / 1024 * 1024;
-  const size_t cap = 200 * 1024;
-  int stages = (int)((cap - 2048) / p.stage_bytes);
+  // Up to ~100 KB of shared memory when five stages fit there, so that the next call's CTA can
+  // take the other half of the SM and stream its weights while this one finishes (programmatic
+  // dependent launch); otherwise one CTA per SM with a deeper ring.
+  int stages = (int)((100 * 1024 - 2048) / p.stage_bytes);
+  if (stages < 5) stages = (int)((200 * 1024 - 2048) / p.stage_bytes);
   if (stages > MAX_STAGES) stages = MAX_STAGES;
   if (stages < 2) return b200_set_error(B200_ERR_UNSUPPORTED, "mx decode: %d tokens do not fit the ring", p.m);
   p.stages = stages;
+  p.nact = stages < PROD_WARPS ? stages : PROD_WARPS;
+  {
+    const int tok = P == 8 ? 1 : 8;
+    const uint32_t read_cols = (uint32_t)((p.m + tok - 1) / tok * tok * P);  // columns the epilogue reads
+    const uint32_t width = ((read_cols > (uint32_t)p.N ? read_cols : (uint32_t)p.N) + 15) / 16 * 16;
+    p.d1_col = width;
+    p.sf_col = 2 * width;
+    const uint32_t need = p.sf_col + 16u * (uint32_t)stages;
+    p.tmem_cols = 32;
+    while (p.tmem_cols < need) p.tmem_cols *= 2;
+    if (p.tmem_cols > 512) return b200_set_error(B200_ERR_UNSUPPORTED, "mx decode: %d tokens exceed tensor memory", p.m);
+  }
   // transaction bytes: the stage's packed codes as stored in global memory (128 rows x 256 codes,
   // one box or two) and the scale box
   p.tx = (uint32_t)(TM * KS * BITS / 8) + (SMODE == SM_E8M0 ? TM * 16 : 0);
@@ -779,6 +620,7 @@ int32_t launch_mx(const LinearArgs &a, cudaStream_t stream) {
   B200_CUDA_TRY(device_sms(&sms));
   if ((size_t)sms * 2 * a.m * TM * sizeof(float) > w->part_bytes)
     return b200_set_error(B200_ERR_UNSUPPORTED, "mx decode: shape beyond the workspace");
+  if (mxs_supported(a)) return launch_mxs(a, *w, stream);
   switch (a.fmt) {
     case B200_FMT_FP4_E2M1: return dispatch<B200_FMT_FP4_E2M1>(a, *w, stream);
     case B200_FMT_FP6_E2M3: return dispatch<B200_FMT_FP6_E2M3>(a, *w, stream);
