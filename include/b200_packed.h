@@ -75,8 +75,11 @@ extern "C" {
 #define B200_PATH_GEMM 2    /* force the tcgen05 GEMM                                   */
 #define B200_PATH_SIMT 3    /* force the fp32 CUDA-core fused kernel                    */
 #define B200_PATH_MX 4      /* force the block-scaled tcgen05 decode kernel: FP4 / FP6
-                               weights (per-32 E8M0, per-row or no scales), bf16 x up to
-                               64 tokens or fp16 x up to 42, K % 256 == 0 */
+                               weights (per-32 E8M0 with K % 512 == 0, per-row or no
+                               scales), bf16 x up to 64 tokens or fp16 x up to 42,
+                               K % 256 == 0. AUTO takes it for FP4 weights at 1..4 tokens
+                               when each SM streams at least 32 (1..2 tokens) or 64
+                               (3..4 tokens) 128-row x 256-deep K stages */
 /* OR-able flag: launch with programmatic dependent launch (PDL). The kernel may start while
  * the previous kernel on the stream is still running; it streams its packed weights and
  * scales at once and waits for that kernel before it reads x or writes y. Only valid when

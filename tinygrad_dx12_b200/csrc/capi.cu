@@ -142,6 +142,7 @@ static int32_t plan(const LinearArgs &a, bool kstride_ok, int32_t path, bool mx_
   switch (path) {
     case B200_PATH_MX: return mx ? B200_PATH_MX : B200_ERR_UNSUPPORTED;
     case B200_PATH_AUTO:
+      if (mx && a.m <= 4 && mx_preferred(a)) return B200_PATH_MX;  // FP4 with many stages per SM
       if (a.m <= 32 && tc) return B200_PATH_GEMV;
       if (a.m > 32 && gm) return B200_PATH_GEMM;
       if (a.m <= 64 && skinny_supported(a)) return B200_PATH_GEMV;  // scales the GEMM declines

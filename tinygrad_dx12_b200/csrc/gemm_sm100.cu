@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         const uint32_t tacc = tmem + (uint32_t)(ab * BT_MAX);
         for (int kb = 0; kb < nk; ++kb, st.next(), ar.next()) {
-          if (!mbar_wait_sleep(&full[st.idx], st.phase, abort_flag) || !mbar_wait_sleep(&aready[ar.idx], ar.phase, abort_flag))
+          if (!mbar_wait(&full[st.idx], st.phase, abort_flag) || !mbar_wait(&aready[ar.idx], ar.phase, abort_flag))
             continue;
           tc_fence_after();
           const uint64_t b0 = sw128_kmajor_desc(xs + st.idx * X_BYTES);

@@ -335,7 +335,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool whole = s0 == 0 && len == p.nst;
       i += len;
       const int buf = seg & 1;
-      if (!mbar_wait_sleep(&accfull[buf], (uint32_t)((seg / 2) & 1), abort_flag)) break;
+      if (!mbar_wait(&accfull[buf], (uint32_t)((seg / 2) & 1), abort_flag)) break;  // no sleep: the tail is latency
       tc_fence_after();
       if (!waited) {  // y, the partials and the tickets belong to the stream order
         asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -380,17 +380,19 @@ __global__ void __launch_bounds__(THREADS, 1)
       ++seg;
       if (!whole) {
         // the last contributor of the tile adds every contributor's partial in CTA order
+        // (the barrier orders every epilogue thread's partial stores before thread 0's fence, which
+        // is cumulative: one gpu-scope fence and an acq_rel ticket publish them all, and the
+        // barrier after the ticket orders the winner's loads after its acquire)
         const int cf = owner(p, (int64_t)t * p.nst), cl = owner(p, (int64_t)t * p.nst + p.nst - 1);
-        __threadfence();
         epi_sync();
         if (threadIdx.x == EPI_WARP0 * 32) {
+          __threadfence();
           unsigned int old;
           asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(old) : "l"(&p.tickets[t]) : "memory");
           *last_flag = old == (unsigned int)(cl - cf) ? 1u : 0u;
         }
         epi_sync();
         if (*last_flag) {
-          __threadfence();
           if (row < p.rows) {
             for (int m0 = 0; m0 < p.m; m0 += 8) {  // 8 tokens at a time: all their loads in flight together
               float sum[8];

@@ -27,9 +27,10 @@
 //     tcgen05.cp right before the stage's four MMAs (copies and MMAs execute in issue order, so
 //     nothing waits for them); the copies rotate over eight column sets, so a copy never
 //     overwrites scales an MMA in flight still reads;
-//   * every loop advances its tile / stage / slot counters incrementally: the MMA thread issues
-//     about one MMA per 36 ns when its loop does no division (measured), against ~21 ns per
-//     MMA of tensor-pipe capacity and ~90 ns per MMA of HBM supply at this N.
+//   * every loop advances its tile / stage / slot counters incrementally (measured: a thread
+//     issues one MMA per ~36 ns in a loop without divisions, ~126 ns with a 64-bit modulo per
+//     unit), and two threads issue the MMAs of alternate units (the tensor pipe takes one
+//     K = 64 MMA per ~21 ns at these N; HBM supplies a 16 KB unit per ~370 ns per SM).
 //
 // Work split (stream-K, as gemv_mx.cu): units = (128-row weight tile, 256-deep K stage), CTA c
 // of the persistent grid takes units [c U / G, (c + 1) U / G); a tile split across CTAs is
@@ -37,22 +38,25 @@
 // order (deterministic). Unit i of a CTA reads K stage (u0 + i) % nst, whose x pieces sit in
 // resident slot i % nst: the first min(units, nst) units of a CTA touch distinct stages.
 //
-// Roles (480 threads): warps 13-14 lane 0 issue the TMA loads of the weight codes (one
-// 128-row x 128-byte box = 256 codes per row per stage, 128-byte swizzle) into a ring; they
-// start before the tensor-memory allocation, so a call launched with programmatic dependent
-// launch streams its first stages while the previous call's CTA on the SM finishes. Warps 8-11
-// convert x into the resident pieces. Warps 4-7 build the weight-scale atoms of alternate
-// units. Warp 12 lane 0 issues the copies and MMAs into one of two fp32 accumulators; warps 0-3
-// read them (tcgen05.ld) and finish the rows. Every wait is bounded (sm100.cuh); on give-up the
-// kernel flags the device error word and returns.
+// Roles (512 threads): two pipelines, for the even and the odd units of the CTA. Warps 14-15
+// lane 0 issue the TMA loads of the weight codes (one 128-row x 128-byte box = 256 codes per row
+// per stage, 128-byte swizzle) into the ring slots of their parity; they start before the
+// tensor-memory allocation, so a call launched with programmatic dependent launch streams its
+// first stages while the previous call's CTA on the SM finishes. Warps 12-13 lane 0 each issue
+// the copies and MMAs of their units into their own pair of fp32 accumulators (one thread issues
+// an MMA with two scale copies about every 70 ns; two threads do so concurrently). Warps 8-11
+// convert x into the resident pieces; warps 4-7 build the weight-scale atoms of alternate
+// units; warps 0-3 read the accumulators (tcgen05.ld), add the two issuers' sums and finish the
+// rows. Every wait is bounded (sm100.cuh); on give-up the kernel flags the device error word and
+// returns.
 #include "mx.cuh"
 
 namespace b200 {
 namespace mxs {
 using namespace mx;
 
-constexpr int EPI_WARP0 = 0, SF_WARP0 = 4, CONV_WARP0 = 8, MMA_WARP = 12, PROD_WARP0 = 13, PROD_WARPS = 2;
-constexpr int THREADS = 15 * 32;
+constexpr int EPI_WARP0 = 0, SF_WARP0 = 4, CONV_WARP0 = 8, MMA_WARP0 = 12, PROD_WARP0 = 14, PROD_WARPS = 2;
+constexpr int THREADS = 16 * 32;
 constexpr int TMEM_THREADS = PROD_WARP0 * 32;  // every warp but the producers
 constexpr int STAGE_BYTES = TM * 128;          // 128 rows x 256 FP4 codes
 constexpr int SFR = 8;                         // scale-factor atom ring (units in flight)
@@ -67,9 +71,10 @@ struct Params {
   int m, N;                 // tokens, MMA N = 8 m
   int stages;               // weight-code ring depth
   int nb;                   // resident x-piece slots: min(max units per CTA, nst)
+  int nmma;                 // MMA issuers (1 or 2): issuer k takes the units i = k (mod nmma)
   uint32_t b_off, sfb_off, sfa_off, bar_off;  // smem: pieces [nb][N][128 B], SFB atoms [nb][512 B],
                                               // SFA atom ring [SFR][2][512 B], barriers
-  uint32_t d1_col, sfa_col, sfb_col, tmem_cols;
+  uint32_t width, sfa_col, sfb_col, tmem_cols;  // accumulator [issuer k][buffer] at (2 k + buffer) * width
   uint32_t idesc;
   const uint16_t *x;        // activations (bf16 or fp16), row stride ldx
   int64_t ldx;
@@ -100,7 +105,7 @@ __device__ __forceinline__ void sf_copy(uint32_t taddr, uint64_t desc) {
 }
 
 template <int SMODE, bool XBF16>
-__global__ void __launch_bounds__(THREADS, 2) mxs_kernel(const __grid_constant__ CUtensorMap tmw, const Params p) {
+__global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__ CUtensorMap tmw, const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t *ring = base;
@@ -112,10 +117,10 @@ __global__ void __launch_bounds__(THREADS, 2) mxs_kernel(const __grid_constant__
   uint64_t *empty = full + S;
   uint64_t *sfready = empty + S;
   uint64_t *sffree = sfready + SFR;
-  uint64_t *accfull = sffree + SFR;
-  uint64_t *accempty = accfull + 2;
-  uint64_t *drain = accempty + 2;
-  uint64_t *bready = drain + 1;  // [nb], one phase each
+  uint64_t *accfull = sffree + SFR;  // [issuer][buffer]
+  uint64_t *accempty = accfull + 4;
+  uint64_t *drain = accempty + 2;  // [issuer]
+  uint64_t *bready = drain + 2;  // [nb], one phase each
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bready + p.nb);
   volatile uint32_t *abort_flag = tmem_slot + 1;
   volatile uint32_t *last_flag = tmem_slot + 2;
@@ -135,11 +140,10 @@ __global__ void __launch_bounds__(THREADS, 2) mxs_kernel(const __grid_constant__
       mbar_init(&sfready[r], 1);
       mbar_init(&sffree[r], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&accfull[b], 1);
-      mbar_init(&accempty[b], 4);
-    }
-    mbar_init(drain, 1);
+    for (int b = 0; b < 4; ++b) mbar_init(&accfull[b], 1);
+    for (int b = 0; b < 2; ++b) mbar_init(&accempty[b], 4);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     for (int b = 0; b < nb; ++b) mbar_init(&bready[b], 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -149,9 +153,11 @@ __global__ void __launch_bounds__(THREADS, 2) mxs_kernel(const __grid_constant__
 
   if (warp >= PROD_WARP0) {
     // ---------------- TMA producers: weight codes (no dependency on the previous kernel) -------
+    // producer pw fills the ring slots of parity pw (the ring depth is even), i.e. the units
+    // i = pw (mod 2): with two MMA issuers, producer k and issuer k form one pipeline
     const int pw = warp - PROD_WARP0;
-    const int nact = S < PROD_WARPS ? S : PROD_WARPS;  // an actor never runs a ring round ahead
-    if (lane == 0 && pw < nact) {
+    const int nact = PROD_WARPS;
+    if (lane == 0) {
       prefetch_tmap(&tmw);
       int t = t0, s = s0 + pw;
       while (s >= nst) s -= nst, ++t;
@@ -173,52 +179,60 @@ __global__ void __launch_bounds__(THREADS, 2) mxs_kernel(const __grid_constant__
     return;  // the producers take no part in the tensor-memory barriers below
   }
 
-  if (warp == MMA_WARP) tmem_alloc(tmem_slot, p.tmem_cols);
+  if (warp == MMA_WARP0) tmem_alloc(tmem_slot, p.tmem_cols);
   tc_fence_before();
   tmem_sync();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= CONV_WARP0 && warp < CONV_WARP0 + 4) {
-    // ---------------- x -> eight FP4 pieces per token, resident slots b = cw (mod 4) -----------
+  if (warp < 4 || (warp >= CONV_WARP0 && warp < CONV_WARP0 + 4)) {
+    // ---------------- x -> eight FP4 pieces per token, resident slots b = cw (mod 8) -----------
+    // Converters: warps 8-11 and the epilogue warps 0-3, which take their epilogue role after.
     // Slot b holds K stage (s0 + b) % nst: B rows 8 mm + c (token mm, piece c) of 128 bytes
     // (128-byte swizzle), and its scale-factor atom (row j: bytes 0-3 = K blocks 0-3 of B row j,
     // bytes 8-11 = K blocks 4-7, so tensor-memory columns c and c + 2 hold the two groups).
-    const int cw = warp - CONV_WARP0;
+    const int cw = warp < 4 ? warp : warp - CONV_WARP0 + 4;  // converter 0..7
     const uint32_t chunk = (uint32_t)lane >> 2, off = (uint32_t)(lane & 3) * 4;
     const int kb = lane >> 2;  // this lane's K block of the stage (elements 8 lane .. 8 lane + 7)
-    for (int b = cw; b < nb; b += 4)  // pad bytes of the atoms: scale 2^0
+    for (int b = cw; b < nb; b += 8)  // pad bytes of the atoms: scale 2^0
       reinterpret_cast<uint4 *>(sfb_atoms + (size_t)b * 512)[lane] = make_uint4(0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
     __syncwarp();
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
-    for (int b = cw; b < nb; b += 4) {
-      int s = s0 + b;
-      if (s >= nst) s -= nst;  // b < nst
-      const uint16_t *xs = p.x + (int64_t)s * KS + 8 * lane;
-      uint8_t *bt = bres + (size_t)b * p.N * 128;
-      uint8_t *atom = sfb_atoms + (size_t)b * 512 + (kb < 4 ? kb : 4 + kb);
-      for (int m0 = 0; m0 < p.m; m0 += 2) {  // two tokens' loads in flight together
-        float v[2][8];
+    // (slot, token) pairs of this warp in slot-major order, four pairs' loads in flight at once
+    const int myslots = nb > cw ? (nb - cw + 7) / 8 : 0;
+    const int pairs = myslots * p.m;
+    for (int q0 = 0; q0 < pairs; q0 += 4) {
+      uint4 raw[4];
 #pragma unroll
-        for (int q = 0; q < 2; ++q)
-          if (m0 + q < p.m) load8<XBF16>(xs + (int64_t)(m0 + q) * p.ldx, v[q]);
+      for (int q = 0; q < 4; ++q) {
+        if (q0 + q >= pairs) break;
+        const int b = cw + 8 * ((q0 + q) / p.m), mm = (q0 + q) % p.m;
+        int s = s0 + b;
+        if (s >= nst) s -= nst;  // b < nst
+        raw[q] = *reinterpret_cast<const uint4 *>(p.x + (int64_t)mm * p.ldx + (int64_t)s * KS + 8 * lane);
+      }
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const int mm = m0 + q;
-          if (mm >= p.m) break;
-          uint32_t pc[8];
-          const uint32_t byte0 = split_fp4<8>(v[q], pc);
+      for (int q = 0; q < 4; ++q) {
+        if (q0 + q >= pairs) break;
+        const int b = cw + 8 * ((q0 + q) / p.m), mm = (q0 + q) % p.m;
+        float v[8];
+        raw_to_f32<XBF16>(raw[q], v);
+        uint32_t pc[8];
+        const uint32_t byte0 = split_fp4<8>(v, pc);
+        uint8_t *bt = bres + (size_t)b * p.N * 128;
+        uint8_t *atom = sfb_atoms + (size_t)b * 512 + (kb < 4 ? kb : 4 + kb);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const uint32_t j = (uint32_t)(mm * 8 + c);  // B row of token mm's piece c
-            *reinterpret_cast<uint32_t *>(bt + j * 128 + ((chunk ^ (j & 7)) << 4) + off) = pc[c];
-            if ((lane & 3) == 0) atom[j * 16] = (uint8_t)(byte0 == 255u ? (c == 0 ? 255u : 127u) : byte0 - 2u * c);
-          }
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t j = (uint32_t)(mm * 8 + c);  // B row of token mm's piece c
+          *reinterpret_cast<uint32_t *>(bt + j * 128 + ((chunk ^ (j & 7)) << 4) + off) = pc[c];
+          if ((lane & 3) == 0) atom[j * 16] = (uint8_t)(byte0 == 255u ? (c == 0 ? 255u : 127u) : byte0 - 2u * c);
+        }
+        if (mm == p.m - 1) {  // the slot's last token: its pieces and scales are ready
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bready[b]);
         }
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bready[b]);
     }
   } else if (warp >= SF_WARP0 && warp < SF_WARP0 + 4) {
     // ---------------- weight scales -> scale-factor atoms, units i = w (mod 4) -----------------
@@ -256,21 +270,23 @@ __global__ void __launch_bounds__(THREADS, 2) mxs_kernel(const __grid_constant__
 #pragma unroll
       for (int q = 0; q < 4; ++q) cur[q] = nxt[q];
     }
-  } else if (warp == MMA_WARP) {
-    // ---------------- MMA issuer: per unit two scale copies and four K = 64 MMAs ----------------
-    if (lane == 0) {
-      const uint32_t d_col[2] = {0u, p.d1_col};
+  } else if (warp >= MMA_WARP0 && warp < MMA_WARP0 + 2) {
+    // ---------------- MMA issuers: per unit two scale copies and four K = 64 MMAs ----------------
+    // Issuer k takes the units i = k (mod nmma) into its own accumulator pair; a tile segment's
+    // result is the sum of the issuers' accumulators. Unit i's segment is (s0 + i) / nst.
+    const int k = warp - MMA_WARP0;
+    if (lane == 0 && k < p.nmma) {
+      const int nm = p.nmma;
       const uint32_t id0 = p.idesc, id2 = p.idesc | (2u << 4) | (2u << 29);  // scale bytes 0-1 | 2-3
       const uint32_t hi = 2u << 30;
-      int slot = 0, r = 0, set = 0, b = 0, s = s0, seg = -1;
+      int slot = k, r = k, set = k, b = k % nst, s = s0 + k, seg = 0;
+      while (s >= nst) s -= nst, ++seg;
       uint32_t round = 0, rround = 0;
-      for (int i = 0; i < n; ++i) {
-        const bool seg_start = i == 0 || s == 0;
-        const bool seg_end = i == n - 1 || s == nst - 1;
-        if (seg_start) {
-          ++seg;
-          if (seg >= 2 && !mbar_wait(&accempty[seg & 1], (uint32_t)((seg / 2 - 1) & 1), abort_flag)) break;
-        }
+      for (int i = k; i < n; i += nm) {
+        const bool first = i < nm || s < nm;              // this issuer's first unit of the segment
+        const bool last = i + nm >= n || s + nm >= nst;   // ... and its last
+        const int buf = seg & 1;
+        if (first && seg >= 2 && !mbar_wait(&accempty[buf], (uint32_t)((seg / 2 - 1) & 1), abort_flag)) break;
         const uint32_t sfb = tmem + p.sfb_col + 4u * (uint32_t)b;
         if (i < nb) {  // first use of resident slot b (== i): its x pieces and their scales
           if (!mbar_wait(&bready[b], 0u, abort_flag)) break;
@@ -285,39 +301,54 @@ __global__ void __launch_bounds__(THREADS, 2) mxs_kernel(const __grid_constant__
         sf_copy(sfa + 4u, sf_atom_desc(sfa_atoms + (size_t)r * 1024 + 512));
         const uint64_t ad = sw128_kmajor_desc(ring + (size_t)slot * STAGE_BYTES);
         const uint64_t bd = sw128_kmajor_desc(bres + (size_t)b * p.N * 128);
-        const uint32_t dcol = tmem + d_col[seg & 1];
-        mma_mxf4(dcol, ad, bd, id0, seg_start ? 0u : 1u, sfa, sfb);
+        const uint32_t dcol = tmem + (uint32_t)(2 * k + buf) * p.width;
+        mma_mxf4(dcol, ad, bd, id0, first ? 0u : 1u, sfa, sfb);
         mma_mxf4(dcol, ad + 2, bd + 2, id2, 1u, sfa | hi, sfb | hi);
         mma_mxf4(dcol, ad + 4, bd + 4, id0, 1u, sfa + 4u, sfb + 2u);
         mma_mxf4(dcol, ad + 6, bd + 6, id2, 1u, (sfa + 4u) | hi, (sfb + 2u) | hi);
         mma_commit(&empty[slot]);
         mma_commit(&sffree[r]);
-        if (seg_end) mma_commit(&accfull[seg & 1]);
-        if (++slot == S) slot = 0, ++round;
-        if (++r == SFR) r = 0, ++rround;
-        set = (set + 1) & 7;
-        if (++b == nst) b = 0;
-        if (++s == nst) s = 0;
+        if (last) mma_commit(&accfull[2 * k + buf]);
+        if ((slot += nm) >= S) slot -= S, ++round;
+        if ((r += nm) >= SFR) r -= SFR, ++rround;
+        set = (set + nm) & 7;
+        b += nm;
+        while (b >= nst) b -= nst;
+        s += nm;
+        while (s >= nst) s -= nst, ++seg;
       }
       // every MMA issued has completed before the CTA frees its tensor memory
-      mma_commit(drain);
-      mbar_wait(drain, 0, abort_flag, 200000000ull);
+      mma_commit(&drain[k]);
+      mbar_wait(&drain[k], 0, abort_flag, 200000000ull);
     }
-  } else {
+  }
+  if (warp < 4) {
     // ---------------- epilogue (warps 0-3): rows of the tile, one per thread ----------------
+    // Whole tiles are stored at once; a tile shared with other CTAs (at most this CTA's first and
+    // last) is published right after its partial sums are stored, and its last contributor adds
+    // every contributor's partial in CTA order. (Publishing both at the end instead measured
+    // slower: the two tickets and reductions then pile up on the same late CTAs.)
     const int r = warp * 32 + lane;  // row within the tile = tensor-memory lane
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const uint32_t d_col[2] = {0u, p.d1_col};
-    bool waited = false;
+    bool waited = false, ok = true;
+    uint32_t ph = 0;  // phase bit of accfull[issuer][buffer]
     int seg = 0;
-    for (int i = 0; i < n;) {
+    for (int i = 0; i < n && ok;) {
       const int64_t u = u0 + i;
       const int t = (int)(u / p.nst), s0 = (int)(u % p.nst);
       const int len = (p.nst - s0) < (n - i) ? (p.nst - s0) : (n - i);
       const bool whole = s0 == 0 && len == p.nst;
-      i += len;
       const int buf = seg & 1;
-      if (!mbar_wait_sleep(&accfull[buf], (uint32_t)((seg / 2) & 1), abort_flag)) break;
+      // issuers with a unit in this segment (units i .. i + len - 1, issuer k has i = k mod nmma)
+      const uint32_t contrib = p.nmma == 1 ? 1u : len >= 2 ? 3u : (1u << (i & 1));
+      i += len;
+      for (int k = 0; k < 2; ++k)
+        if (contrib >> k & 1u) {
+          const int a = 2 * k + buf;
+          ok = ok && mbar_wait(&accfull[a], (ph >> a) & 1u, abort_flag);  // no sleep: the tail is latency
+          ph ^= 1u << a;
+        }
+      if (!ok) break;
       tc_fence_after();
       if (!waited) {  // y, the partials and the tickets belong to the stream order
         asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -330,9 +361,13 @@ __global__ void __launch_bounds__(THREADS, 2) mxs_kernel(const __grid_constant__
       const int e = (u0 / p.nst == t) ? 0 : 1;  // this CTA's first or last tile
       float *mypart = p.part + ((size_t)blockIdx.x * 2 + e) * p.m * TM;
       for (int mm = 0; mm < p.m; ++mm) {
-        float v[8];
-        tmem_ld_x8(tmem + lane_base + d_col[buf] + 8u * (uint32_t)mm, v);  // token mm's eight pieces
-        const float acc = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+        float acc = 0.f;
+        for (int k = 0; k < 2; ++k)
+          if (contrib >> k & 1u) {
+            float v[8];  // token mm's eight pieces in issuer k's accumulator
+            tmem_ld_x8(tmem + lane_base + (uint32_t)(2 * k + buf) * p.width + 8u * (uint32_t)mm, v);
+            acc += ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+          }
         if (whole) {
           if (row < p.rows) {
             const float yv = acc * rs;
@@ -347,59 +382,65 @@ __global__ void __launch_bounds__(THREADS, 2) mxs_kernel(const __grid_constant__
       __syncwarp();
       if (lane == 0) mbar_arrive(&accempty[buf]);
       ++seg;
-      if (!whole) {
-        // the last contributor of the tile adds every contributor's partial in CTA order
-        const int cf = owner(p, (int64_t)t * p.nst), cl = owner(p, (int64_t)t * p.nst + p.nst - 1);
+      if (whole) continue;
+      // (the barrier orders every epilogue thread's partial stores before thread 0's fence, which
+      // is cumulative: one gpu-scope fence and the acq_rel ticket publish them all, and the
+      // barrier after the ticket orders the winner's loads after thread 0's acquire)
+      const int cf = owner(p, (int64_t)t * p.nst), cl = owner(p, (int64_t)t * p.nst + p.nst - 1);
+      epi_sync();
+      if (threadIdx.x == EPI_WARP0 * 32) {
         __threadfence();
-        epi_sync();
-        if (threadIdx.x == EPI_WARP0 * 32) {
-          unsigned int old;
-          asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(old) : "l"(&p.tickets[t]) : "memory");
-          *last_flag = old == (unsigned int)(cl - cf) ? 1u : 0u;
-        }
-        epi_sync();
-        if (*last_flag) {
-          __threadfence();
-          if (row < p.rows) {
-            float sum[MAX_M];
-#pragma unroll
-            for (int q = 0; q < MAX_M; ++q) sum[q] = 0.f;
-            for (int cc = cf; cc <= cl; ++cc) {
-              const int ee = (unit_start(p, cc) / p.nst == t) ? 0 : 1;
-              const float *src = p.part + ((size_t)cc * 2 + ee) * p.m * TM + r;
-              float v[MAX_M];
-#pragma unroll
-              for (int q = 0; q < MAX_M; ++q) v[q] = q < p.m ? __ldcg(src + (size_t)q * TM) : 0.f;
-#pragma unroll
-              for (int q = 0; q < MAX_M; ++q) sum[q] += v[q];
-            }
-#pragma unroll
-            for (int q = 0; q < MAX_M; ++q) {
-              if (q >= p.m) break;
-              const float yv = sum[q] * rs;
-              store_f32(p.y, q * p.ldy_m + row, p.ydt, yv);
-              for (int cp = 0; cp < p.ncopy; ++cp) store_f32(p.ycopy[cp], q * p.ldy_m + row, p.ydt, yv);
-            }
-          }
-          if (threadIdx.x == EPI_WARP0 * 32) p.tickets[t] = 0u;  // ready for the next call
-        }
-        epi_sync();
+        unsigned int old;
+        asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(old) : "l"(&p.tickets[t]) : "memory");
+        *last_flag = old == (unsigned int)(cl - cf) ? 1u : 0u;
       }
+      epi_sync();
+      if (*last_flag) {
+        if (row < p.rows) {
+          float sum[MAX_M];
+#pragma unroll
+          for (int q = 0; q < MAX_M; ++q) sum[q] = 0.f;
+          for (int c0 = cf; c0 <= cl; c0 += 4) {  // four contributors' loads in flight, summed in CTA order
+            float v[4][MAX_M];
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              const int cc = c0 + jj;
+              const int ee = cc <= cl && (unit_start(p, cc) / p.nst == t) ? 0 : 1;
+              const float *src = p.part + ((size_t)cc * 2 + ee) * p.m * TM + r;
+#pragma unroll
+              for (int q = 0; q < MAX_M; ++q) v[jj][q] = (cc <= cl && q < p.m) ? __ldcg(src + (size_t)q * TM) : 0.f;
+            }
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+              for (int q = 0; q < MAX_M; ++q) sum[q] += v[jj][q];
+          }
+#pragma unroll
+          for (int q = 0; q < MAX_M; ++q) {
+            if (q >= p.m) break;
+            const float yv = sum[q] * rs;
+            store_f32(p.y, q * p.ldy_m + row, p.ydt, yv);
+            for (int cp = 0; cp < p.ncopy; ++cp) store_f32(p.ycopy[cp], q * p.ldy_m + row, p.ydt, yv);
+          }
+        }
+        if (threadIdx.x == EPI_WARP0 * 32) p.tickets[t] = 0u;  // ready for the next call
+      }
+      epi_sync();
     }
   }
   tc_fence_before();
   tmem_sync();
   tc_fence_after();
-  if (warp == MMA_WARP) tmem_dealloc(tmem, p.tmem_cols);
+  if (warp == MMA_WARP0) tmem_dealloc(tmem, p.tmem_cols);
 }
 
-// Shared-memory layout and ring depth (stages == 0: the resident slots do not fit), and the
-// tensor-memory columns: two accumulators of `width`, SFR sets of 8 SFA columns, 4 SFB columns
-// per resident slot.
+// Shared-memory layout and even ring depth (stages == 0: the resident slots do not fit), and
+// the tensor-memory columns: four accumulators of `width` ([issuer][buffer]), SFR sets of 8 SFA
+// columns, 4 SFB columns per resident slot (256 or 512 columns; one CTA per SM).
 struct Layout {
   int stages, nb;
   uint32_t b_off, sfb_off, sfa_off, bar_off;
-  uint32_t width, sfa_col, sfb_col;
+  uint32_t width, sfa_col, sfb_col, tmem_cols;
   size_t smem;
 };
 
@@ -408,22 +449,20 @@ static Layout layout_for(int64_t units, int grid, int nst, int N) {
   const int64_t nmax = (units + grid - 1) / grid;
   l.nb = (int)(nmax < nst ? nmax : nst);
   l.width = N <= 16 ? 16u : 32u;
-  l.sfa_col = 2 * l.width;
+  l.sfa_col = 4 * l.width;
   l.sfb_col = l.sfa_col + 8 * SFR;
-  if (l.sfb_col + 4u * (uint32_t)l.nb > 256) return Layout{};
+  const uint32_t need = l.sfb_col + 4u * (uint32_t)l.nb;
+  if (need > 512) return Layout{};
+  l.tmem_cols = need <= 256 ? 256u : 512u;
   const size_t bbytes = (size_t)l.nb * N * 128, sfbbytes = (size_t)l.nb * 512, sfabytes = (size_t)SFR * 1024;
   auto total = [&](int s) {
-    const size_t bars = 8 * (2 * (size_t)s + 2 * SFR + 5 + l.nb) + 16;
+    const size_t bars = 8 * (2 * (size_t)s + 2 * SFR + 4 + 2 + 2 + l.nb) + 16;
     return 1024 + (size_t)s * STAGE_BYTES + bbytes + sfbbytes + sfabytes + bars;
   };
-  // two CTAs per SM when at least four stages fit in ~113 KB (the next call's CTA then streams
-  // its first stages while this one finishes); else one CTA with a deeper ring
+  // one CTA per SM (shared memory above half the SM's): two CTAs of one grid on an SM would
+  // split its bandwidth while another SM idles (measured: a ~5 us tail at c2 with ~113 KB CTAs)
   int s = 0;
-  while (s < MAX_STAGES && total(s + 1) <= 113 * 1024) ++s;
-  if (s < 4) {
-    s = 0;
-    while (s < MAX_STAGES && total(s + 1) <= 200 * 1024) ++s;
-  }
+  while (s + 2 <= MAX_STAGES && total(s + 2) <= 200 * 1024) s += 2;
   if (s < 2) return Layout{};
   l.stages = s;
   l.b_off = (uint32_t)s * STAGE_BYTES;
@@ -431,6 +470,7 @@ static Layout layout_for(int64_t units, int grid, int nst, int N) {
   l.sfa_off = l.sfb_off + (uint32_t)sfbbytes;
   l.bar_off = l.sfa_off + (uint32_t)sfabytes;
   l.smem = total(s);
+  if (l.smem < 116 * 1024) l.smem = 116 * 1024;
   return l;
 }
 
@@ -456,10 +496,14 @@ static int32_t launch_t(const LinearArgs &a, const Workspace &w, cudaStream_t st
   p.sfb_off = l.sfb_off;
   p.sfa_off = l.sfa_off;
   p.bar_off = l.bar_off;
-  p.d1_col = l.width;
+  p.width = l.width;
   p.sfa_col = l.sfa_col;
   p.sfb_col = l.sfb_col;
-  p.tmem_cols = 256;
+  p.tmem_cols = l.tmem_cols;
+  // two issuers unless a CTA wraps around K with an odd stage count (a resident slot would then
+  // be used by both issuers, and its scale copy is ordered only within one issuer's stream)
+  const int64_t nmax = (p.units + p.grid - 1) / p.grid;
+  p.nmma = (nmax <= p.nst || p.nst % 2 == 0) ? 2 : 1;
   // kind::mxf4: A and B E2M1 (format 1), E8M0 scales, M = 128, N = 8 m
   p.idesc = (1u << 7) | (1u << 10) | ((uint32_t)(p.N >> 3) << 17) | (1u << 23) | ((uint32_t)(TM >> 4) << 24);
   p.x = static_cast<const uint16_t *>(a.x);
@@ -510,6 +554,23 @@ bool mxs_supported(const LinearArgs &a) {
   const int64_t units = ((a.rows + TM - 1) / TM) * (int64_t)nst;
   const int grid = (int)(units < sms ? units : sms);
   return layout_for(units, grid, nst, 8 * (int)a.m).stages != 0;
+}
+
+// Whether the automatic path should take this kernel over the mma.sync decode GEMV: only when
+// every CTA streams enough stages to amortise the fixed costs of a call (x conversion, scale
+// atoms, the split-tile fixup; about 4 us). Measured, FP4 E8M0 bf16, units per CTA in
+// brackets: 57344 x 8192 [97] M=1 45.6 vs 50.0 us, M=2 48.7 vs 62.1, M=4 76.3 vs 92.5;
+// 8192 x 28672 [48] M=1 29.6 vs 36.5, M=2 34.0 vs 114, M=4 48.3 vs 44.3; 10240 x 8192 [18]
+// M=1 16.6 vs 16.1; 8192 x 8192 [14] M=1 16.6 vs 10.7.
+bool mx_preferred(const LinearArgs &a) {
+  using namespace mxs;
+  if (!mxs_supported(a)) return false;
+  int sms = 0;
+  if (device_sms(&sms) != cudaSuccess) return false;
+  const int64_t units = ((a.rows + TM - 1) / TM) * (a.cols / KS);
+  const int64_t grid = units < sms ? units : sms;
+  const int64_t per_cta = (units + grid - 1) / grid;
+  return a.m <= 2 ? per_cta >= 32 : per_cta >= 64;
 }
 
 int32_t launch_mxs(const LinearArgs &a, const mx::Workspace &w, cudaStream_t stream) {

@@ -66,6 +66,8 @@ bool mx_ready(cudaStream_t stream);  // its workspace exists or can be allocated
 int32_t launch_mx(const LinearArgs &a, cudaStream_t stream);
 int32_t mx_device_error(unsigned int *v, bool clear);
 int32_t mx_reset_tickets();  // after a device error: zero the split-tile tickets on this device
+// the resident-pieces FP4 kernel (gemv_mxs.cu) for 1..4 tokens is faster than the decode GEMV here
+bool mx_preferred(const LinearArgs &a);
 
 // dense fp16 / bf16 tcgen05 GEMM for ordinary matmuls (gemm_dense.cu): c = a @ b with a
 // row-major (k contiguous) and b K-major (k contiguous per column), fp32 accumulation

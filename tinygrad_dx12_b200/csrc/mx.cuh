@@ -170,6 +170,22 @@ __device__ __forceinline__ void mma_mxf4(uint32_t tmem_d, uint64_t adesc, uint64
       : "memory");
 }
 
+// 8 activations (one 16-byte load of bf16 or fp16) as float.
+template <bool XBF16>
+__device__ __forceinline__ void raw_to_f32(const uint4 raw, float (&v)[8]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (XBF16) {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    } else {
+      v[2 * i] = __half2float(__ushort_as_half((unsigned short)(w[i] & 0xFFFFu)));
+      v[2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(w[i] >> 16)));
+    }
+  }
+}
+
 template <bool XBF16>
 __device__ __forceinline__ void load8(const uint16_t *src, float (&v)[8]) {
   const uint4 raw = *reinterpret_cast<const uint4 *>(src);
