@@ -237,3 +237,24 @@ def test_dtype_argument_and_cast_call_forms(m, dt):
     ulp = 2.0 ** (-8 if dt == torch.bfloat16 else -11)
     diff = (y_dtype.float() - y_cast.float()).abs()
     assert torch.all(diff <= ulp * y_cast.float().abs() * 2 + 1e-30)
+
+
+def test_profile_hook_reports_kernel_and_estimates():
+    """set_profile_hook sees every matmul with the kernel that ran and its Estimates."""
+    import tinygrad_dx12_b200 as tg
+
+    rng = np.random.default_rng(11)
+    spec = ref.make_packed(rng, "fp4_e2m1", 256, 512, 32, "e8m0")
+    w = to_device(spec, "cuda:0", "e8m0")
+    x = torch.randn((2, 512), device="cuda:0").to(torch.bfloat16)
+    seen = []
+    tg.set_profile_hook(lambda kernel, est: seen.append((kernel, est)))
+    try:
+        tg.matmul(w, x.t(), dtype=torch.bfloat16)
+        tg.matmul(w, x.t(), scope="tiled", dtype=torch.bfloat16)
+    finally:
+        tg.set_profile_hook(None)
+    torch.cuda.synchronize()
+    assert [k for k, _ in seen][1] == "generic" and seen[0][0] in ("mx", "gemv", "gemm", "simt")
+    assert seen[0][1] == tg.estimates(w, x.t(), dtype=torch.bfloat16)
+    assert seen[0][1].ops == 2 * 256 * 2 * 512

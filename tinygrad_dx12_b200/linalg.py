@@ -22,11 +22,13 @@ The fused call form is ``matmul(W, x.T)`` with ``W`` a ``PackedTensor`` of shape
 
 from __future__ import annotations
 
+from typing import NamedTuple
+
 import torch
 
 from . import _lib
 from . import dtypes as D
-from .packed import PackedTensor, matrix_intermediate, stream_ptr, ctypes_ref
+from .packed import FORMATS, PackedTensor, matrix_intermediate, stream_ptr, ctypes_ref
 
 SCOPES = ("auto", "Wave", "ThreadGroup", "tiled")
 FUSED_IO = (torch.float16, torch.bfloat16, torch.float32)
@@ -155,6 +157,58 @@ def choose_matrix(w: PackedTensor, x_dtype: torch.dtype, m: int, out_dtype: torc
     return ("tiled", None)
 
 
+class Estimates(NamedTuple):
+    """Cost of one matrix product, for profilers (the reference attaches
+    ``Estimates(2*m*n*k, bytes)`` to its LinAlg program, codegen/linalg.py:50-56).
+
+    ``ops`` and ``mem`` follow the reference: 2·m·n·k, and the output plus both operands at
+    the dtypes its matrix program sees them (a packed operand as the decoded intermediate).
+    ``packed_mem`` is what the fused kernels move instead: packed codes, scales, the other
+    operand and the output, each read or written once."""
+
+    ops: int
+    mem: int
+    packed_mem: int
+
+
+def estimates(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor,
+              dtype: torch.dtype | None = None) -> Estimates:
+    """Estimates of ``matmul(a, b, dtype=dtype)`` (shapes and dtypes only; no device work)."""
+    if len(a.shape) != 2 or len(b.shape) != 2 or a.shape[1] != b.shape[0]:
+        raise ValueError("matrix operands must have compatible rank-two shapes")
+    intermediate = matrix_intermediate(a, b)
+    m, k, n = a.shape[0], a.shape[1], b.shape[1]
+    lhs_dt = intermediate if isinstance(a, PackedTensor) else a.dtype
+    rhs_dt = intermediate if isinstance(b, PackedTensor) else b.dtype
+    out_dt = dtype or D.accumulator(lhs_dt, rhs_dt)
+    size = lambda dt: torch.empty((), dtype=dt).element_size()  # noqa: E731
+    mem = m * n * size(out_dt) + m * k * size(lhs_dt) + k * n * size(rhs_dt)
+
+    def moved(op, rows, cols, dt):
+        if isinstance(op, PackedTensor):
+            scales = 0 if op.scales is None else op.scales.numel() * op.scales.element_size()
+            return -(-op.shape[0] * op.shape[1] * FORMATS[op.format][0] // 8) + scales
+        return rows * cols * size(dt)
+
+    packed = m * n * size(out_dt) + moved(a, m, k, lhs_dt) + moved(b, k, n, rhs_dt)
+    return Estimates(2 * m * n * k, mem, packed)
+
+
+_profile_hook = None
+
+
+def set_profile_hook(hook) -> None:
+    """Install ``hook(kernel, estimates)`` (or None): called after every ``matmul`` launch with
+    the kernel that ran ('mx', 'gemv', 'gemm', 'simt' or 'generic') and its Estimates."""
+    global _profile_hook
+    _profile_hook = hook
+
+
+def _report(kernel: str, a, b, dtype) -> None:
+    if _profile_hook is not None:
+        _profile_hook(kernel, estimates(a, b, dtype))
+
+
 def matmul(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor, scope: str = "auto",
            tile: tuple[int, int, int] | None = None, dtype: torch.dtype | None = None) -> torch.Tensor:
     """Multiply two matrices on the B200 device (linalg.py:136-223).
@@ -188,14 +242,19 @@ def matmul(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor, scope
             w, x = fused
             if automatic:  # one library call: it picks the kernel or reports that none fits
                 try:
-                    return _packed_linear(w, x, out_dtype, "auto").t()
+                    y = _packed_linear(w, x, out_dtype, "auto").t()
+                    if _profile_hook is not None:
+                        _report(linear_plan(w, x.dtype, x.shape[0], out_dtype) or "auto", a, b, dtype)
+                    return y
                 except _lib.B200Error as error:
                     if error.code != _lib.ERR_UNSUPPORTED:
                         raise
             else:
                 for path in _SCOPE_PATHS[scope]:
                     if linear_plan(w, x.dtype, x.shape[0], out_dtype, path) is not None:
-                        return _packed_linear(w, x, out_dtype, path).t()
+                        y = _packed_linear(w, x, out_dtype, path).t()
+                        _report(path, a, b, dtype)
+                        return y
         if not automatic:
             raise RuntimeError(f"B200 {scope} {tile} rejected: no fused kernel for these operands")
     # ordinary compute: decode to the intermediate, then the generic matmul
@@ -203,7 +262,9 @@ def matmul(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor, scope
     lhs = a.unpack(wide) if isinstance(a, PackedTensor) else a
     rhs = b.unpack(wide) if isinstance(b, PackedTensor) else b
     acc = D.sum_acc_dtype(out_dtype) if D.is_float(out_dtype) else out_dtype
-    return _generic_matmul(lhs, rhs, out_dtype, acc)
+    y = _generic_matmul(lhs, rhs, out_dtype, acc)
+    _report("generic", a, b, dtype)
+    return y
 
 
 def matvec(matrix: torch.Tensor | PackedTensor, vector: torch.Tensor, output_dtype: torch.dtype | None = None,
