@@ -818,7 +818,8 @@ def profile_case(case: str, launches: int):
     """Small untimed workload for ncu captures: `launches` plain b200_packed_linear calls.
 
     gemv: c2 M=1 over 4 resident weight copies (143 MB > L2); skinny: the same at M=8;
-    gemm: c3 M=4096 (one weight).
+    gemm: c3 M=4096 (one weight); mx: the c5 gate|up projection at TP=1 (57344 x 8192 FP4,
+    E8M0, M=1; the automatic path takes the block-scaled tcgen05 kernel there), 2 copies.
     Nothing is timed; the process only has to exit 0 so the same command line can be profiled.
     """
     import torch
@@ -826,11 +827,13 @@ def profile_case(case: str, launches: int):
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    cfg = dict(GEMV_CFG if case in ("gemv", "skinny") else GEMM_CFG)
+    cfg = dict(GEMV_CFG if case in ("gemv", "skinny", "mx") else GEMM_CFG)
     if case == "skinny":
         cfg["m"] = 8
+    if case == "mx":
+        cfg["n"] = 57344
     xdt = getattr(torch, cfg["xdt"])
-    ws = make_weights(cfg, device, 1 if case == "gemm" else 4, seed=0)
+    ws = make_weights(cfg, device, 1 if case == "gemm" else 2 if case == "mx" else 4, seed=0)
     x = (torch.randn((cfg["m"], cfg["k"]), device=device) / 8).to(xdt)
     y = torch.empty((cfg["m"], cfg["n"]), device=device, dtype=xdt)
     code = _lib.DT[cfg["xdt"]]
@@ -856,7 +859,7 @@ def main():
     ap.add_argument("--no-configs", action="store_true", help="skip the c1 / c2 M=8,32 / c5 M=2048 / c4 legs")
     ap.add_argument("--stack-layers", type=int, default=None, help="layers of the c5 stack leg (default: all 80)")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
-    ap.add_argument("--profile-case", choices=["gemv", "skinny", "gemm"], default=None,
+    ap.add_argument("--profile-case", choices=["gemv", "skinny", "gemm", "mx"], default=None,
                     help="run a small untimed workload for ncu and exit")
     ap.add_argument("--launches", type=int, default=6, help="launches of --profile-case")
     args = ap.parse_args()
