@@ -98,15 +98,17 @@ def test_repeated_calls_and_pdl_flag():
         assert torch.equal(o, y0)
 
 
-def test_x_blocks_with_zeros_and_wide_range():
-    """Blocks of x that are all zero (scale byte 127), values spanning 2^-20..2^20 inside one
-    block (the low pieces leave the E4M3 range: error below 2^-17 of the block maximum)."""
+@pytest.mark.parametrize("m", [1, 2])
+def test_x_blocks_with_zeros_and_wide_range(m):
+    """Blocks of x that are all zero, values spanning 2^-20..2^20 inside one block: the error
+    stays below 2^-17 of the block maximum (several tokens: per-block piece scales) or of the
+    vector maximum (one token: the row-split kernel's single scale)."""
     from tinygrad_dx12_b200.linalg import _packed_linear
 
     spec = _spec("fp4_e2m1", 512, 4096, 32, "e8m0", 7)
     w = to_device(spec, DEV, "e8m0")
     rng = np.random.default_rng(8)
-    xv = rng.standard_normal((2, 4096)) * np.exp2(rng.integers(-20, 21, size=(2, 4096)))
+    xv = rng.standard_normal((m, 4096)) * np.exp2(rng.integers(-20, 21, size=(m, 4096)))
     xv[:, 64:128] = 0.0
     x = torch.from_numpy(xv.astype(np.float32)).to(DEV).to(torch.bfloat16)
     y = _packed_linear(w, x, torch.float32, "mx").cpu().numpy()

@@ -104,6 +104,33 @@ __device__ __forceinline__ uint32_t split_pieces(float (&v)[8], uint2 (&out)[P])
   return byte;
 }
 
+// The NP FP4 E2M1 pieces of 8 values under a given E8M0 scale byte of piece 0 (piece q: byte - 2q):
+// piece 0 rounds r / 2^(byte-127) to E2M1, each later piece the remainder at a quarter of the
+// previous scale. out[q] holds the 8 codes (low nibble = lower element). With |r| < 4 * 2^(byte-127)
+// the error after NP pieces is at most 2^(byte-127-2NP).
+template <int NP>
+__device__ __forceinline__ void fp4_pieces(float (&r)[8], uint32_t byte, uint32_t (&out)[NP]) {
+  float inv = __uint_as_float((254u - byte) << 23), scale = __uint_as_float(byte << 23);
+#pragma unroll
+  for (int q = 0; q < NP; ++q) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const __nv_fp4x2_storage_t c =
+          __nv_cvt_float2_to_fp4x2(make_float2(r[2 * h] * inv, r[2 * h + 1] * inv), __NV_E2M1, cudaRoundNearest);
+      w |= (uint32_t)c << (8 * h);
+      if (q + 1 < NP) {
+        const __half2_raw back = __nv_cvt_fp4x2_to_halfraw2(c, __NV_E2M1);
+        r[2 * h] -= __half2float(__ushort_as_half(back.x)) * scale;
+        r[2 * h + 1] -= __half2float(__ushort_as_half(back.y)) * scale;
+      }
+    }
+    out[q] = w;
+    inv *= 4.f;
+    scale *= 0.25f;
+  }
+}
+
 // Split 8 activations (one lane's share of a 32-element block, 4 lanes per block) into NP FP4
 // E2M1 pieces. Piece 0 takes the E8M0 block scale 2^e that puts the block maximum in [2, 4),
 // where the E2M1 grid step is 1, so its rounding error is at most 2^(e-1); piece q takes scale
@@ -137,25 +164,7 @@ __device__ __forceinline__ uint32_t split_fp4(float (&r)[8], uint32_t (&out)[NP]
   }
   const int b = ilogbf(amax) + 126;  // scale 2^(ilogb-1): the maximum lands in [2, 4)
   const uint32_t byte = (uint32_t)(b < 2 * NP - 1 ? 2 * NP - 1 : b > 253 ? 253 : b);
-  float inv = __uint_as_float((254u - byte) << 23), scale = __uint_as_float(byte << 23);
-#pragma unroll
-  for (int q = 0; q < NP; ++q) {
-    uint32_t w = 0;
-#pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const __nv_fp4x2_storage_t c =
-          __nv_cvt_float2_to_fp4x2(make_float2(r[2 * h] * inv, r[2 * h + 1] * inv), __NV_E2M1, cudaRoundNearest);
-      w |= (uint32_t)c << (8 * h);
-      if (q + 1 < NP) {
-        const __half2_raw back = __nv_cvt_fp4x2_to_halfraw2(c, __NV_E2M1);
-        r[2 * h] -= __half2float(__ushort_as_half(back.x)) * scale;
-        r[2 * h + 1] -= __half2float(__ushort_as_half(back.y)) * scale;
-      }
-    }
-    out[q] = w;
-    inv *= 4.f;
-    scale *= 0.25f;
-  }
+  fp4_pieces<NP>(r, byte, out);
   return byte;
 }
 
@@ -224,5 +233,8 @@ int32_t workspace_for(cudaStream_t stream, bool may_allocate, Workspace *&out);
 // the resident-pieces kernel for FP4 weights and 1..4 tokens (gemv_mxs.cu); the caller has
 // checked mx_supported
 bool mxs_supported(const LinearArgs &a);
+// the row-split kernel for FP4 weights at one token, K <= 8192 (gemv_mxr.cu)
+bool mxr_supported(const LinearArgs &a);
+int32_t launch_mxr(const LinearArgs &a, cudaStream_t stream);
 int32_t launch_mxs(const LinearArgs &a, const mx::Workspace &w, cudaStream_t stream);
 }  // namespace b200
