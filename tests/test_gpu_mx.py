@@ -101,8 +101,8 @@ def test_repeated_calls_and_pdl_flag():
 @pytest.mark.parametrize("m", [1, 2])
 def test_x_blocks_with_zeros_and_wide_range(m):
     """Blocks of x that are all zero, values spanning 2^-20..2^20 inside one block: the error
-    stays below 2^-17 of the block maximum (several tokens: per-block piece scales) or of the
-    vector maximum (one token: the row-split kernel's single scale)."""
+    of the per-block piece scales stays below 2^-17 of the block maximum, at one token and at
+    two."""
     from tinygrad_dx12_b200.linalg import _packed_linear
 
     spec = _spec("fp4_e2m1", 512, 4096, 32, "e8m0", 7)

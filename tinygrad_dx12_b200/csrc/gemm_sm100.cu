@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         const uint32_t tacc = tmem + (uint32_t)(ab * BT_MAX);
         for (int kb = 0; kb < nk; ++kb, st.next(), ar.next()) {
-          if (!mbar_wait(&full[st.idx], st.phase, abort_flag) || !mbar_wait(&aready[ar.idx], ar.phase, abort_flag))
+          if (!mbar_wait_sleep(&full[st.idx], st.phase, abort_flag) || !mbar_wait_sleep(&aready[ar.idx], ar.phase, abort_flag))
             continue;
           tc_fence_after();
           const uint64_t b0 = sw128_kmajor_desc(xs + st.idx * X_BYTES);
@@ -387,23 +387,6 @@ int32_t make_tma_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, 
   CUresult r = fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return b200_set_error(B200_ERR_CUDA, "cuTensorMapEncodeTiled failed: %d", (int)r);
-  return B200_OK;
-}
-
-// 3-D tiled TMA descriptor: dims {inner, d1, d2} with byte strides d1_stride, d2_stride (each a
-// multiple of 16), box {box0, box1, box2}; the box lands as [box2][box1][box0] in shared memory.
-int32_t make_tma_3d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t d1,
-                    uint64_t d2, uint64_t d1_stride, uint64_t d2_stride, uint32_t box0, uint32_t box1, uint32_t box2,
-                    CUtensorMapSwizzle swz) {
-  auto fn = gemm::encode_fn();
-  if (!fn) return b200_set_error(B200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  const cuuint64_t dims[3] = {inner, d1, d2};
-  const cuuint64_t strides[2] = {d1_stride, d2_stride};
-  const cuuint32_t box[3] = {box0, box1, box2};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, dt, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return b200_set_error(B200_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed: %d", (int)r);
   return B200_OK;
 }
 

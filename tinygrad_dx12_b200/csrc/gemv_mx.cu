@@ -622,7 +622,6 @@ int32_t launch_mx(const LinearArgs &a, cudaStream_t stream) {
   B200_CUDA_TRY(device_sms(&sms));
   if ((size_t)sms * 2 * a.m * TM * sizeof(float) > w->part_bytes)
     return b200_set_error(B200_ERR_UNSUPPORTED, "mx decode: shape beyond the workspace");
-  if (mxr_supported(a)) return launch_mxr(a, stream);
   if (mxs_supported(a)) return launch_mxs(a, *w, stream);
   switch (a.fmt) {
     case B200_FMT_FP4_E2M1: return dispatch<B200_FMT_FP4_E2M1>(a, *w, stream);

@@ -46,12 +46,6 @@ int32_t gemm_device_error(unsigned int *v, bool clear);
 int32_t make_tma_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
 
-// 3-D tiled TMA descriptor (gemm_sm100.cu): dims {inner, d1, d2}, byte strides of d1 and d2
-// (multiples of 16), box lands as [box2][box1][box0]
-int32_t make_tma_3d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t d1,
-                    uint64_t d2, uint64_t d1_stride, uint64_t d2_stride, uint32_t box0, uint32_t box1, uint32_t box2,
-                    CUtensorMapSwizzle swz);
-
 // streamed (TMA) decode GEMV for M <= 2 (gemv.cu)
 bool gemv_stream_supported(const LinearArgs &a);
 int32_t launch_gemv_stream(const LinearArgs &a, cudaStream_t stream);

@@ -233,8 +233,5 @@ int32_t workspace_for(cudaStream_t stream, bool may_allocate, Workspace *&out);
 // the resident-pieces kernel for FP4 weights and 1..4 tokens (gemv_mxs.cu); the caller has
 // checked mx_supported
 bool mxs_supported(const LinearArgs &a);
-// the row-split kernel for FP4 weights at one token, K <= 8192 (gemv_mxr.cu)
-bool mxr_supported(const LinearArgs &a);
-int32_t launch_mxr(const LinearArgs &a, cudaStream_t stream);
 int32_t launch_mxs(const LinearArgs &a, const mx::Workspace &w, cudaStream_t stream);
 }  // namespace b200

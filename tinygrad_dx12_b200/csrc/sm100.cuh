@@ -118,15 +118,6 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
-// 3-D TMA tile load (coordinates x, y, z), completion via the mbarrier's transaction count.
-__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int32_t x, int32_t y, int32_t z,
-                                            uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
-          smem_u32(dst)),
-      "l"((uint64_t)map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-      : "memory");
-}
 // 2-D TMA tile store from this CTA's shared memory (bulk-group completion); elements outside the
 // tensor are not written. Coordinates must be non-negative.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int32_t x, int32_t y) {
