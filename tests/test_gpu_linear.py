@@ -258,3 +258,32 @@ def test_profile_hook_reports_kernel_and_estimates():
     assert [k for k, _ in seen][1] == "generic" and seen[0][0] in ("mx", "gemv", "gemm", "simt")
     assert seen[0][1] == tg.estimates(w, x.t(), dtype=torch.bfloat16)
     assert seen[0][1].ops == 2 * 256 * 2 * 512
+
+
+@pytest.mark.parametrize("afmt,akind,bfmt,bkind", [("fp4_e2m1", None, "fp4_e2m1", None),
+                                                   ("fp6_e3m2", "e8m0", "fp4_e2m1", None),
+                                                   ("fp4_e2m1", "e8m0", "fp6_e2m3", "e8m0")])
+@pytest.mark.parametrize("n", [1, 3, 64, 300])
+def test_packed_pair_runs_fused(afmt, akind, bfmt, bkind, n):
+    """Packed x packed (dx12.py:115-138): the right operand's FP4 / FP6 codes (unscaled or E8M0)
+    decode exactly to bf16 and the product runs on the fused tensor-core kernels with the left
+    operand as the weights; the result matches the oracle's float32 product of both decodes, in
+    the float32 accumulator dtype. The tiled scope keeps the ordinary kernel."""
+    import tinygrad_dx12_b200 as tg
+
+    sa = _spec(afmt, 256, 512, 32, akind, 21)
+    sb = _spec(bfmt, 512, n, 32, bkind, 22)
+    a = to_device(sa, DEV, "e8m0" if akind else None)
+    b = to_device(sb, DEV, "e8m0" if bkind else None)
+    seen = []
+    tg.set_profile_hook(lambda kernel, est: seen.append(kernel))
+    try:
+        y = tg.matmul(a, b)
+        yt = tg.matmul(a, b, scope="tiled")
+    finally:
+        tg.set_profile_hook(None)
+    torch.cuda.synchronize()
+    assert y.dtype == torch.float32 and seen[0] in ("mx", "gemv", "gemm", "simt") and seen[1] == "generic"
+    r = _wref(sa, "e8m0" if akind else None) @ _wref(sb, "e8m0" if bkind else None)
+    assert_close(y.cpu().numpy(), r, "float32")
+    assert_close(yt.float().cpu().numpy(), r, "float32")

@@ -81,10 +81,25 @@ def _generic_matmul(lhs: torch.Tensor, rhs: torch.Tensor, out_dtype: torch.dtype
     return out.view(out_dtype) if fp8_out else out
 
 
+_EXACT_IN_BF16 = ("fp4_e2m1", "fp6_e2m3", "fp6_e3m2")
+
+
 def _fused_operands(a, b, out_dtype):
-    """The (W, x) pair for a fused call, or None when the fused kernels cannot take it."""
-    if not isinstance(a, PackedTensor) or isinstance(b, PackedTensor) or len(a.shape) != 2:
+    """The (W, x) pair for a fused call, or None when the fused kernels cannot take it.
+
+    A packed right operand (the packed x packed products, dx12.py:115-138) is decoded to bf16
+    first when that is exact: FP4 / FP6 codes, unscaled or with E8M0 scales (at most 4
+    significant bits times a power of two inside bf16's range). The left operand then runs
+    through the fused kernels as the weights (its codes read by the tensor cores)."""
+    if not isinstance(a, PackedTensor) or len(a.shape) != 2:
         return None
+    if isinstance(b, PackedTensor):
+        exact = b.format in _EXACT_IN_BF16 and (b.scales is None or b.scales.dtype == torch.float8_e8m0fnu)
+        if not exact or len(b.shape) != 2 or out_dtype not in FUSED_IO:
+            return None
+        if a.scales is not None and D.name(a.scales.dtype) == "float64":
+            return None
+        return a, b.unpack(torch.bfloat16).t()  # x[m, k] = b[k, m], exact
     if b.dtype not in FUSED_IO or out_dtype not in FUSED_IO:
         return None
     if a.scales is not None and D.name(a.scales.dtype) == "float64":
