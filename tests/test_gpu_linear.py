@@ -287,3 +287,33 @@ def test_packed_pair_runs_fused(afmt, akind, bfmt, bkind, n):
     r = _wref(sa, "e8m0" if akind else None) @ _wref(sb, "e8m0" if bkind else None)
     assert_close(y.cpu().numpy(), r, "float32")
     assert_close(yt.float().cpu().numpy(), r, "float32")
+
+
+@pytest.mark.parametrize("m,fmt,sk", [(1, "fp4_e2m1", "e8m0"), (2, "fp4_e2m1", "e8m0"), (8, "int4", "f16u"),
+                                      (64, "fp6_e3m2", "f16row")])
+def test_host_activation_and_out(m, fmt, sk):
+    """Pinned host x and a pinned host out (decode steps fed from and returning to the host):
+    the result equals the all-device call bit for bit (same kernel), whether the kernel stores
+    into out itself (decode kernels) or through a device buffer (the GEMM)."""
+    import tinygrad_dx12_b200 as tg
+
+    spec = _spec(fmt, 1024, 2048, 2048 if sk == "f16row" else 32, sk, 31)
+    w = to_device(spec, DEV, "e8m0" if sk == "e8m0" else None)
+    xdt = torch.bfloat16 if sk == "e8m0" else torch.float16
+    xd = torch.randn((m, 2048), device=DEV).to(xdt)
+    ref_y = tg.matmul(w, xd.t(), dtype=xdt)
+    xh = xd.cpu().pin_memory()
+    yh = torch.full((m, 1024), float("nan"), dtype=xdt).pin_memory()
+    for _ in range(2):  # the staging buffer and out reused across calls
+        got = tg.matmul(w, xh.t(), dtype=xdt, out=yh.t())
+        torch.cuda.synchronize()
+        assert got.data_ptr() == yh.data_ptr()
+        assert torch.equal(yh, ref_y.t().cpu())
+    yd = torch.empty((1024, m), device=DEV, dtype=xdt)
+    assert tg.matmul(w, xh.t(), dtype=xdt, out=yd) is yd
+    torch.cuda.synchronize()
+    assert torch.equal(yd.cpu(), ref_y.cpu())
+    with pytest.raises(ValueError):
+        tg.matmul(w, xd.cpu().t(), dtype=xdt)  # host operand not pinned
+    with pytest.raises(ValueError):
+        tg.matmul(w, xh.t(), dtype=xdt, out=torch.empty((1024, m), dtype=torch.float32).pin_memory())

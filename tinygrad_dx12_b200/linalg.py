@@ -127,15 +127,19 @@ def _aligned_x(x: torch.Tensor) -> torch.Tensor:
     return buf[:, :k]
 
 
-def _packed_linear(w: PackedTensor, x: torch.Tensor, out_dtype: torch.dtype, path: str, flags: int = 0) -> torch.Tensor:
-    """y[M, N] = x[M, K] @ dequant(W)[N, K]^T through ``b200_packed_linear`` (``flags``: B200_FLAG_*)."""
+def _packed_linear(w: PackedTensor, x: torch.Tensor, out_dtype: torch.dtype, path: str, flags: int = 0,
+                   y: torch.Tensor | None = None) -> torch.Tensor:
+    """y[M, N] = x[M, K] @ dequant(W)[N, K]^T through ``b200_packed_linear`` (``flags``: B200_FLAG_*);
+    ``y``, when given, is the destination (unit column stride)."""
     x = _aligned_x(x)
     m = x.shape[0]
     ldx = x.stride(0) if m > 1 else -(-x.shape[1] // 8) * 8
-    y = torch.empty((m, w.rows), device=x.device, dtype=out_dtype)
+    if y is None:
+        y = torch.empty((m, w.rows), device=x.device, dtype=out_dtype)
     d = w.desc()
     _lib.call("b200_packed_linear", ctypes_ref(d), x.data_ptr(), _lib.DT[D.name(x.dtype)], m, ldx, 1,
-              y.data_ptr(), _lib.DT[D.name(out_dtype)], y.stride(0), 1, _lib.PATH[path] | flags, stream_ptr(x.device))
+              y.data_ptr(), _lib.DT[D.name(out_dtype)], y.stride(0) if m > 1 else w.rows, 1, _lib.PATH[path] | flags,
+              stream_ptr(x.device))
     return y
 
 
@@ -224,18 +228,108 @@ def _report(kernel: str, a, b, dtype) -> None:
         _profile_hook(kernel, estimates(a, b, dtype))
 
 
+# decode kernels that store y with plain stores (the GEMMs write it with TMA stores), so y may be
+# a pinned host buffer
+_HOST_Y_PLANS = ("gemv", "mx", "simt")
+
+
+_STAGING: dict = {}  # (device, stream, dtype) -> device buffer reused by every staged call on that stream
+
+
+def _stage_host(t: torch.Tensor, device: torch.device) -> torch.Tensor:
+    """A pinned host tensor on ``device``: for 16/32-bit floats laid out row- or column-major, the
+    library's copy kernel reads it over the host link (for a decode step's few KB this costs a
+    few microseconds, well under a DMA copy's setup) into a buffer kept per stream (calls on one
+    stream run in order, so the next call's copy starts after this call's kernel has read it);
+    anything else goes through ``to``."""
+    if not t.is_pinned():
+        raise ValueError("a host matrix operand must be in pinned memory (torch.Tensor.pin_memory())")
+    tt = t.t()
+    src = t if t.is_contiguous() else tt if tt.is_contiguous() else None
+    if src is None or t.dtype not in FUSED_IO:
+        return t.to(device, non_blocking=True)
+    stream = stream_ptr(device)
+    key = (device.index, stream, src.dtype)
+    buf = _STAGING.get(key)
+    n = src.numel()
+    if buf is None or buf.numel() < n:
+        buf = torch.empty(max(n, 1 << 14), device=device, dtype=src.dtype)
+        _STAGING[key] = buf
+    dst = buf[:n].view(src.shape)
+    code = _lib.DT[D.name(src.dtype)]
+    _lib.call("b200_cast", src.data_ptr(), code, dst.data_ptr(), code, n, stream)
+    return dst if src is t else dst.t()
+
+
+def _host_decode_step(a: PackedTensor, b: torch.Tensor, dtype, out):
+    """The lean form of the host-I/O call for a decode step, or None when it does not apply:
+    b = x.T with x (M, K) pinned and row-major, ``dtype`` given, out = y.T with y (M, N) pinned
+    and row-major (or None), and a decode kernel (plain stores) as the plan. Two library calls:
+    the staging copy of x and the fused kernel storing into y."""
+    if dtype not in FUSED_IO or b.dtype not in FUSED_IO or b.dim() != 2 or len(a.shape) != 2:
+        return None
+    kdim, m = b.shape
+    if a.shape[1] != kdim or kdim % 8 or b.stride(0) != 1 or (m > 1 and b.stride(1) != kdim) or b.storage_offset():
+        return None
+    n = a.shape[0]
+    if out is not None and (out.device.type != "cpu" or out.dtype != dtype or tuple(out.shape) != (n, m)
+                            or out.stride(0) != 1 or (m > 1 and out.stride(1) != n)):
+        return None
+    if a.scales is not None and a.scales.dtype == torch.float64:
+        return None
+    plans = a.__dict__.setdefault("_plans", {})
+    pkey = (b.dtype, m, dtype)
+    if pkey not in plans:
+        plans[pkey] = linear_plan(a, b.dtype, m, dtype)
+    path = plans[pkey]
+    if path not in _HOST_Y_PLANS:
+        return None
+    if not b.is_pinned() or (out is not None and not out.is_pinned()):
+        raise ValueError("host matrix operands must be in pinned memory (torch.Tensor.pin_memory())")
+    device = a.data.device
+    stream = stream_ptr(device)
+    key = (device.index, stream, b.dtype)
+    buf = _STAGING.get(key)
+    if buf is None or buf.numel() < m * kdim:
+        buf = torch.empty(max(m * kdim, 1 << 14), device=device, dtype=b.dtype)
+        _STAGING[key] = buf
+    xcode, ycode = _lib.DT[D.name(b.dtype)], _lib.DT[D.name(dtype)]
+    _lib.call("b200_cast", b.data_ptr(), xcode, buf.data_ptr(), xcode, m * kdim, stream)
+    y = torch.empty((m, n), device=device, dtype=dtype) if out is None else out
+    _lib.call("b200_packed_linear", ctypes_ref(a.desc()), buf.data_ptr(), xcode, m, kdim, 1, y.data_ptr(), ycode, n,
+              1, _lib.PATH[path], stream)
+    if _profile_hook is not None:
+        _report(path, a, b, dtype)
+    return out if out is not None else y.t()
+
+
 def matmul(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor, scope: str = "auto",
-           tile: tuple[int, int, int] | None = None, dtype: torch.dtype | None = None) -> torch.Tensor:
+           tile: tuple[int, int, int] | None = None, dtype: torch.dtype | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
     """Multiply two matrices on the B200 device (linalg.py:136-223).
 
     Packed operands decode inside the fused kernels; other combinations decode with
     ``b200_dequant`` to the common intermediate and multiply with the generic kernel.
     ``dtype`` declares the output precision (accumulation is float32 in the fused kernels,
     the output dtype's reduction type in the generic one). No gradients are defined.
+
+    Host I/O for decode steps whose tokens arrive from and return to the host (no counterpart
+    in the reference): ``b`` may be a pinned host tensor, staged onto ``a``'s device by a small
+    library kernel, and ``out`` a tensor of the result's shape and dtype (pinned host or on the
+    device) that receives the result -- the decode kernels store into a pinned ``out`` directly
+    when its transpose is contiguous, other paths go through a device buffer and a copy. Both
+    are asynchronous on the current stream: synchronize before reading ``out``, and keep the
+    host tensors alive until then.
     """
     if scope not in SCOPES:
         raise ValueError(f"unknown matrix scope {scope!r}")
     automatic = scope == "auto"
+    if isinstance(b, torch.Tensor) and b.device.type == "cpu" and _device_of(a).type == "cuda":
+        if automatic and tile is None and isinstance(a, PackedTensor):
+            y = _host_decode_step(a, b, dtype, out)
+            if y is not None:
+                return y
+        b = _stage_host(b, _device_of(a))
     device, other_device = _device_of(a), _device_of(b)
     if device != other_device:
         raise ValueError("matrix operands must belong to one device")
@@ -249,15 +343,29 @@ def matmul(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor, scope
     lhs_dt = intermediate if isinstance(a, PackedTensor) else a.dtype
     rhs_dt = intermediate if isinstance(b, PackedTensor) else b.dtype
     out_dtype = dtype or D.accumulator(lhs_dt, rhs_dt)
+    if out is not None and (tuple(out.shape) != (m, n) or out.dtype != out_dtype):
+        raise ValueError(f"out must be a {out_dtype} tensor of shape {(m, n)}")
+    if out is not None and out.device.type == "cpu" and not out.is_pinned():
+        raise ValueError("a host out tensor must be in pinned memory (torch.Tensor.pin_memory())")
     if 0 in (m, k, n):
-        return torch.zeros((m, n), device=device, dtype=out_dtype)
+        return _deliver(torch.zeros((m, n), device=device, dtype=out_dtype), out)
     if scope != "tiled":
         fused = _fused_operands(a, b, out_dtype)
         if fused is not None:
             w, x = fused
+            if automatic and out is not None and (out.device.type == "cpu" or out.device == device) \
+                    and out.t().is_contiguous():
+                plans = w.__dict__.setdefault("_plans", {})  # the plan depends on shapes and dtypes only
+                pkey = (x.dtype, x.shape[0], out_dtype)
+                path = plans.get(pkey, "") if pkey in plans else plans.setdefault(
+                    pkey, linear_plan(w, x.dtype, x.shape[0], out_dtype))
+                if path is not None and (out.device == device or path in _HOST_Y_PLANS):
+                    _packed_linear(w, x, out_dtype, path, y=out.t())  # the kernel stores into out itself
+                    _report(path, a, b, dtype)
+                    return out
             if automatic:  # one library call: it picks the kernel or reports that none fits
                 try:
-                    y = _packed_linear(w, x, out_dtype, "auto").t()
+                    y = _deliver(_packed_linear(w, x, out_dtype, "auto").t(), out)
                     if _profile_hook is not None:
                         _report(linear_plan(w, x.dtype, x.shape[0], out_dtype) or "auto", a, b, dtype)
                     return y
@@ -267,7 +375,7 @@ def matmul(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor, scope
             else:
                 for path in _SCOPE_PATHS[scope]:
                     if linear_plan(w, x.dtype, x.shape[0], out_dtype, path) is not None:
-                        y = _packed_linear(w, x, out_dtype, path).t()
+                        y = _deliver(_packed_linear(w, x, out_dtype, path).t(), out)
                         _report(path, a, b, dtype)
                         return y
         if not automatic:
@@ -277,9 +385,16 @@ def matmul(a: torch.Tensor | PackedTensor, b: torch.Tensor | PackedTensor, scope
     lhs = a.unpack(wide) if isinstance(a, PackedTensor) else a
     rhs = b.unpack(wide) if isinstance(b, PackedTensor) else b
     acc = D.sum_acc_dtype(out_dtype) if D.is_float(out_dtype) else out_dtype
-    y = _generic_matmul(lhs, rhs, out_dtype, acc)
+    y = _deliver(_generic_matmul(lhs, rhs, out_dtype, acc), out)
     _report("generic", a, b, dtype)
     return y
+
+
+def _deliver(y: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:
+    if out is None:
+        return y
+    out.copy_(y, non_blocking=True)
+    return out
 
 
 def matvec(matrix: torch.Tensor | PackedTensor, vector: torch.Tensor, output_dtype: torch.dtype | None = None,
