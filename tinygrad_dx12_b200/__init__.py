@@ -7,8 +7,9 @@ Importing the package registers the backend without opening hardware, as
 from .compat import register as register
 from .packed import FORMATS, FP8_CANDIDATES, PackedTensor, matrix_intermediate
 from .linalg import Estimates, choose_matrix, estimates, matmul, matvec, set_profile_hook
+from .graph import GraphStep
 
 register()
 
 __all__ = ["register", "FORMATS", "FP8_CANDIDATES", "PackedTensor", "matrix_intermediate", "matmul", "matvec",
-           "choose_matrix", "Estimates", "estimates", "set_profile_hook"]
+           "choose_matrix", "Estimates", "estimates", "set_profile_hook", "GraphStep"]
