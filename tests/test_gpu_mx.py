@@ -49,8 +49,9 @@ def _run(spec, sdt, m, xdt, ydt, seed=0, xscale=1.0, flags=0):
 
 @pytest.mark.parametrize("m", [1, 2, 3, 8, 16, 32, 33, 64])
 def test_c2_fp4_e8m0(m):
-    """Config c2 (FP4 E2M1 8192 x 8192, per-32 E8M0, bf16 x / y): 64 tiles x 32 stages over 148
-    CTAs, so every tile is shared by two or three CTAs."""
+    """Config c2 (FP4 E2M1 8192 x 8192, per-32 E8M0, bf16 x / y): 64 tiles x 32 stages; at 1..4
+    tokens two CTAs of a cluster take a tile's K halves, above that 148 CTAs share the tiles
+    (stream-K)."""
     _run(_spec("fp4_e2m1", 8192, 8192, 32, "e8m0", 2), "e8m0", m, "bfloat16", "bfloat16")
 
 
@@ -64,12 +65,16 @@ def test_formats_scales_x_dtypes(fmt, kind, sdt, xdt, m):
 
 
 @pytest.mark.parametrize("rows,cols", [(128, 512), (129, 512), (300, 1536), (256, 8192), (4768, 1024),
-                                       (57344, 8192)])
+                                       (57344, 8192), (9600, 1024), (9472, 2048)])
 @pytest.mark.parametrize("m", [1, 4])
 def test_stream_k_splits(rows, cols, m):
-    """Ragged rows, few stages, tiles shared by dozens of CTAs (256 x 8192: 64 units for 148
-    SMs, one unit each) and the c5 gate|up shape (448 tiles x 32 stages). Per-32 E8M0 scales
-    need K % 512 == 0 here (a 16-byte row of scale bytes per TMA box)."""
+    """Both work splits of the 1..4-token FP4 kernel. Pair split (two CTAs per 128-row tile, the
+    second pushing its partials to the first through distributed shared memory; matrices of at
+    most 74 tiles with an even stage count): ragged rows, one to 38 tiles, 2 to 32 stages, and
+    9472 x 2048 with its 148 CTAs filling every SM. Stream-K with tickets: 9600 x 1024 (75 tiles,
+    300 units over 148 CTAs) and the c5 gate|up shape (448 tiles x 32 stages); odd stage counts
+    (unscaled K = 256) in test_single_stage_unscaled. Per-32 E8M0 scales need K % 512 == 0 here (a 16-byte row of scale bytes
+    per TMA box)."""
     _run(_spec("fp4_e2m1", rows, cols, 32, "e8m0", 4), "e8m0", m, "bfloat16", "bfloat16")
 
 

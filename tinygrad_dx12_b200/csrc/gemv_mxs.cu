@@ -37,6 +37,12 @@
 // finished by its last contributor (acquire-release ticket) adding the fp32 partials in CTA
 // order (deterministic). Unit i of a CTA reads K stage (u0 + i) % nst, whose x pieces sit in
 // resident slot i % nst: the first min(units, nst) units of a CTA touch distinct stages.
+// Pair split (matrices of at most SMs / 2 tiles, an even stage count): the grid is two CTAs per
+// tile, launched as 2-CTA clusters, CTA 2t + h taking K half h of tile t (the same unit ranges
+// as stream-K over that grid). The second CTA pushes its fp32 partials into the first one's
+// shared memory (st.shared::cluster, one release-arrive per thread on the first CTA's mbarrier)
+// and the first adds them after its own, in the stream-K order: no global partials, fence or
+// ticket, whose dependent L2 round trips made up most of a one-token call's tail.
 //
 // Roles (512 threads): two pipelines, for the even and the odd units of the CTA. Warps 14-15
 // lane 0 issue the TMA loads of the weight codes (one 128-row x 128-byte box = 256 codes per row
@@ -61,7 +67,8 @@ constexpr int TMEM_THREADS = PROD_WARP0 * 32;  // every warp but the producers
 constexpr int STAGE_BYTES = TM * 128;          // 128 rows x 256 FP4 codes
 constexpr int SFR = 8;                         // scale-factor atom ring (units in flight)
 constexpr int MAX_M = 4;
-constexpr int MAX_STAGES = 8;
+constexpr int MAX_STAGES = 12;
+constexpr int SMEM_MAX = 227 * 1024;            // dynamic shared memory a CTA may take
 
 struct Params {
   int64_t rows, cols;
@@ -72,7 +79,7 @@ struct Params {
   int stages;               // weight-code ring depth
   int nb;                   // resident x-piece slots: min(max units per CTA, nst)
   int nmma;                 // MMA issuers (1 or 2): issuer k takes the units i = k (mod nmma)
-  uint32_t b_off, sfb_off, sfa_off, bar_off;  // smem: pieces [nb][N][128 B], SFB atoms [nb][512 B],
+  uint32_t b_off, sfb_off, sfa_off, bar_off;  // smem: pieces [nb][N][128 B], SFB atoms every N x 16 B,
                                               // SFA atom ring [SFR][2][512 B], barriers
   uint32_t width, sfa_col, sfb_col, tmem_cols;  // accumulator [issuer k][buffer] at (2 k + buffer) * width
   uint32_t idesc;
@@ -89,6 +96,8 @@ struct Params {
   int ncopy;
   float *part;              // [grid][2][m][128] fp32 partials of split tiles
   unsigned int *tickets;    // [ntiles]
+  int pair;                 // pair split (2-CTA clusters), see above
+  uint32_t pair_off;        // smem: [MAX_M][128] fp32 partials pushed by the cluster partner
 };
 
 __device__ __forceinline__ void tmem_sync() { asm volatile("bar.sync 2, %0;" ::"n"(TMEM_THREADS) : "memory"); }
@@ -102,6 +111,56 @@ __device__ __forceinline__ uint64_t sf_atom_desc(const void *atom) {
 // Copy one atom into 4 tensor-memory columns of every lane quarter (row l -> lane l of each).
 __device__ __forceinline__ void sf_copy(uint32_t taddr, uint64_t desc) {
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
+}
+
+// ---- 2-CTA cluster helpers of the pair split ----
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of both CTAs arrives once per phase and waits once per phase (non-aligned forms:
+// the threads of a warp reach them at different points).
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+// This CTA's shared-memory address `a` as seen in the shared window of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t map_rank(uint32_t a, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t a, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t a) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(a) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (the arrivals come from the partner CTA).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, volatile uint32_t *abort_flag) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 63) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > 2000000000ull) {
+        *abort_flag = 1;
+        atomicOr(&g_device_error, B200_DEVERR_MBAR_TIMEOUT);
+        return false;
+      }
+    }
+  }
 }
 
 template <int SMODE, bool XBF16>
@@ -121,7 +180,8 @@ __global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__
   uint64_t *accempty = accfull + 4;
   uint64_t *drain = accempty + 2;  // [issuer]
   uint64_t *bready = drain + 2;  // [nb], one phase each
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bready + p.nb);
+  uint64_t *pairbar = bready + p.nb;  // pair split: the partner's 128 pushes
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pairbar + 1);
   volatile uint32_t *abort_flag = tmem_slot + 1;
   volatile uint32_t *last_flag = tmem_slot + 2;
 
@@ -145,10 +205,15 @@ __global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__
     mbar_init(&drain[0], 1);
     mbar_init(&drain[1], 1);
     for (int b = 0; b < nb; ++b) mbar_init(&bready[b], 1);
+    mbar_init(pairbar, TM);
     *abort_flag = 0;
     fence_mbar_init();
   }
   __syncthreads();
+  // pair split: phase 0 of the cluster barrier publishes the initialised mbarriers to the
+  // partner (waited for before the first remote access); phase 1 at the end keeps this CTA's
+  // shared memory alive until the partner is done with it
+  if (p.pair) cluster_arrive();
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp >= PROD_WARP0) {
@@ -176,8 +241,14 @@ __global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__
           if (q + S >= i) mbar_wait(&full[q % S], (uint32_t)((q / S) & 1), abort_flag, 200000000ull);
       }
     }
+    if (p.pair) {
+      cluster_wait();
+      cluster_arrive();
+      cluster_wait();
+    }
     return;  // the producers take no part in the tensor-memory barriers below
   }
+  bool cluster_phase0 = false;  // pair split: this thread has waited for phase 0
 
   if (warp == MMA_WARP0) tmem_alloc(tmem_slot, p.tmem_cols);
   tc_fence_before();
@@ -194,8 +265,12 @@ __global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__
     const int cw = warp < 4 ? warp : warp - CONV_WARP0 + 4;  // converter 0..7
     const uint32_t chunk = (uint32_t)lane >> 2, off = (uint32_t)(lane & 3) * 4;
     const int kb = lane >> 2;  // this lane's K block of the stage (elements 8 lane .. 8 lane + 7)
-    for (int b = cw; b < nb; b += 8)  // pad bytes of the atoms: scale 2^0
-      reinterpret_cast<uint4 *>(sfb_atoms + (size_t)b * 512)[lane] = make_uint4(0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
+    // An atom's rows 0..N-1 are B rows; the copy also reads its rows N..31, which land in
+    // tensor-memory lanes no MMA of N columns reads, so atom b + 1 starts N rows after atom b.
+    const uint32_t sfbs = (uint32_t)p.N * 16;
+    for (int b = cw; b < nb; b += 8)  // pad bytes of the atoms' B rows: scale 2^0
+      if (lane < p.N)
+        reinterpret_cast<uint4 *>(sfb_atoms + (size_t)b * sfbs)[lane] = make_uint4(0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
     __syncwarp();
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x is the previous kernel's output
     // (slot, token) pairs of this warp in slot-major order, four pairs' loads in flight at once
@@ -211,21 +286,29 @@ __global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__
         if (s >= nst) s -= nst;  // b < nst
         raw[q] = *reinterpret_cast<const uint4 *>(p.x + (int64_t)mm * p.ldx + (int64_t)s * KS + 8 * lane);
       }
+      // the four pairs' pieces are computed before any is stored, so their dependency chains
+      // (eight pieces each) overlap; the conversion is on the path to the first MMA
+      uint32_t pc[4][8], byte0[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (q0 + q < pairs) {  // warp-uniform
+          float v[8];
+          raw_to_f32<XBF16>(raw[q], v);
+          byte0[q] = split_fp4<8>(v, pc[q]);
+        }
+      }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         if (q0 + q >= pairs) break;
         const int b = cw + 8 * ((q0 + q) / p.m), mm = (q0 + q) % p.m;
-        float v[8];
-        raw_to_f32<XBF16>(raw[q], v);
-        uint32_t pc[8];
-        const uint32_t byte0 = split_fp4<8>(v, pc);
         uint8_t *bt = bres + (size_t)b * p.N * 128;
-        uint8_t *atom = sfb_atoms + (size_t)b * 512 + (kb < 4 ? kb : 4 + kb);
+        uint8_t *atom = sfb_atoms + (size_t)b * sfbs + (kb < 4 ? kb : 4 + kb);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const uint32_t j = (uint32_t)(mm * 8 + c);  // B row of token mm's piece c
-          *reinterpret_cast<uint32_t *>(bt + j * 128 + ((chunk ^ (j & 7)) << 4) + off) = pc[c];
-          if ((lane & 3) == 0) atom[j * 16] = (uint8_t)(byte0 == 255u ? (c == 0 ? 255u : 127u) : byte0 - 2u * c);
+          *reinterpret_cast<uint32_t *>(bt + j * 128 + ((chunk ^ (j & 7)) << 4) + off) = pc[q][c];
+          if ((lane & 3) == 0)
+            atom[j * 16] = (uint8_t)(byte0[q] == 255u ? (c == 0 ? 255u : 127u) : byte0[q] - 2u * c);
         }
         if (mm == p.m - 1) {  // the slot's last token: its pieces and scales are ready
           fence_proxy_async_smem();
@@ -238,7 +321,8 @@ __global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__
     // ---------------- weight scales -> scale-factor atoms, units i = w (mod 4) -----------------
     // Unit i's two atoms (K blocks 0-3 and 4-7 of its stage): row l = the words of tile rows
     // l, l + 32, l + 64, l + 96, i.e. tensor-memory columns q = row / 32 of lane row % 32.
-    // The next unit's scale loads are issued before this unit's atoms are written.
+    // The next unit's scale loads are issued before this unit's atoms are written (keeping more
+    // in flight measured slower: they delay the x loads that the first MMA waits for).
     const int sw = warp - SF_WARP0;
     int t = t0, s = s0 + sw;
     while (s >= nst) s -= nst, ++t;
@@ -291,7 +375,7 @@ __global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__
         if (i < nb) {  // first use of resident slot b (== i): its x pieces and their scales
           if (!mbar_wait(&bready[b], 0u, abort_flag)) break;
           tc_fence_after();
-          sf_copy(sfb, sf_atom_desc(sfb_atoms + (size_t)b * 512));
+          sf_copy(sfb, sf_atom_desc(sfb_atoms + (size_t)b * p.N * 16));
         }
         if (!mbar_wait(&sfready[r], rround & 1u, abort_flag)) break;
         if (!mbar_wait(&full[slot], round & 1u, abort_flag)) break;
@@ -331,6 +415,12 @@ __global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__
     const int r = warp * 32 + lane;  // row within the tile = tensor-memory lane
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     bool waited = false, ok = true;
+    const uint32_t prank = p.pair ? cluster_rank() : 0u;
+    float *pairbuf = reinterpret_cast<float *>(base + p.pair_off);
+    if (p.pair) {
+      cluster_wait();
+      cluster_phase0 = true;
+    }
     uint32_t ph = 0;  // phase bit of accfull[issuer][buffer]
     int seg = 0;
     for (int i = 0; i < n && ok;) {
@@ -360,6 +450,9 @@ __global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__
         if (row < p.rows) rs = load_as_f32(p.rscale, row, p.sdt);
       const int e = (u0 / p.nst == t) ? 0 : 1;  // this CTA's first or last tile
       float *mypart = p.part + ((size_t)blockIdx.x * 2 + e) * p.m * TM;
+      float mine[MAX_M];
+#pragma unroll
+      for (int q = 0; q < MAX_M; ++q) mine[q] = 0.f;
       for (int mm = 0; mm < p.m; ++mm) {
         float acc = 0.f;
         for (int k = 0; k < 2; ++k)
@@ -374,6 +467,11 @@ __global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__
             store_f32(p.y, mm * p.ldy_m + row, p.ydt, yv);
             for (int cp = 0; cp < p.ncopy; ++cp) store_f32(p.ycopy[cp], mm * p.ldy_m + row, p.ydt, yv);
           }
+        } else if (p.pair) {
+          if (prank == 1u) st_cluster_f32(map_rank(smem_u32(pairbuf + mm * TM + r), 0u), acc);
+#pragma unroll
+          for (int q = 0; q < MAX_M; ++q)
+            if (q == mm) mine[q] = acc;
         } else {
           mypart[(size_t)mm * TM + r] = acc;
         }
@@ -383,6 +481,26 @@ __global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__
       if (lane == 0) mbar_arrive(&accempty[buf]);
       ++seg;
       if (whole) continue;
+      if (p.pair) {
+        // second half: publish this thread's pushes; first half: add them after its own sums
+        if (prank == 1u) {
+          mbar_arrive_cluster(map_rank(smem_u32(pairbar), 0u));
+        } else {
+          ok = mbar_wait_cluster(pairbar, 0u, abort_flag);
+          if (ok && row < p.rows) {
+            for (int mm = 0; mm < p.m; ++mm) {
+              float mv = 0.f;
+#pragma unroll
+              for (int q = 0; q < MAX_M; ++q)
+                if (q == mm) mv = mine[q];
+              const float yv = (mv + pairbuf[mm * TM + r]) * rs;
+              store_f32(p.y, mm * p.ldy_m + row, p.ydt, yv);
+              for (int cp = 0; cp < p.ncopy; ++cp) store_f32(p.ycopy[cp], mm * p.ldy_m + row, p.ydt, yv);
+            }
+          }
+        }
+        continue;
+      }
       // (the barrier orders every epilogue thread's partial stores before thread 0's fence, which
       // is cumulative: one gpu-scope fence and the acq_rel ticket publish them all, and the
       // barrier after the ticket orders the winner's loads after thread 0's acquire)
@@ -432,6 +550,11 @@ __global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__
   tmem_sync();
   tc_fence_after();
   if (warp == MMA_WARP0) tmem_dealloc(tmem, p.tmem_cols);
+  if (p.pair) {
+    if (!cluster_phase0) cluster_wait();
+    cluster_arrive();
+    cluster_wait();
+  }
 }
 
 // Shared-memory layout and even ring depth (stages == 0: the resident slots do not fit), and
@@ -439,7 +562,7 @@ __global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__
 // columns, 4 SFB columns per resident slot (256 or 512 columns; one CTA per SM).
 struct Layout {
   int stages, nb;
-  uint32_t b_off, sfb_off, sfa_off, bar_off;
+  uint32_t b_off, sfb_off, sfa_off, pair_off, bar_off;
   uint32_t width, sfa_col, sfb_col, tmem_cols;
   size_t smem;
 };
@@ -454,24 +577,36 @@ static Layout layout_for(int64_t units, int grid, int nst, int N) {
   const uint32_t need = l.sfb_col + 4u * (uint32_t)l.nb;
   if (need > 512) return Layout{};
   l.tmem_cols = need <= 256 ? 256u : 512u;
-  const size_t bbytes = (size_t)l.nb * N * 128, sfbbytes = (size_t)l.nb * 512, sfabytes = (size_t)SFR * 1024;
+  const size_t bbytes = (size_t)l.nb * N * 128, sfbbytes = (size_t)(l.nb - 1) * N * 16 + 512;
+  const size_t sfabytes = (size_t)SFR * 1024;
+  const size_t pairbytes = (size_t)MAX_M * TM * 4;
   auto total = [&](int s) {
-    const size_t bars = 8 * (2 * (size_t)s + 2 * SFR + 4 + 2 + 2 + l.nb) + 16;
-    return 1024 + (size_t)s * STAGE_BYTES + bbytes + sfbbytes + sfabytes + bars;
+    const size_t bars = 8 * (2 * (size_t)s + 2 * SFR + 4 + 2 + 2 + l.nb + 1) + 16;
+    return 1024 + (size_t)s * STAGE_BYTES + bbytes + sfbbytes + sfabytes + pairbytes + bars;
   };
   // one CTA per SM (shared memory above half the SM's): two CTAs of one grid on an SM would
   // split its bandwidth while another SM idles (measured: a ~5 us tail at c2 with ~113 KB CTAs)
   int s = 0;
-  while (s + 2 <= MAX_STAGES && total(s + 2) <= 200 * 1024) s += 2;
+  while (s + 2 <= MAX_STAGES && total(s + 2) <= (size_t)SMEM_MAX) s += 2;
   if (s < 2) return Layout{};
   l.stages = s;
   l.b_off = (uint32_t)s * STAGE_BYTES;
   l.sfb_off = l.b_off + (uint32_t)bbytes;
   l.sfa_off = l.sfb_off + (uint32_t)sfbbytes;
-  l.bar_off = l.sfa_off + (uint32_t)sfabytes;
+  l.pair_off = l.sfa_off + (uint32_t)sfabytes;
+  l.bar_off = l.pair_off + (uint32_t)pairbytes;
   l.smem = total(s);
   if (l.smem < 116 * 1024) l.smem = 116 * 1024;
   return l;
+}
+
+// Pair split: an even stage count and two CTAs per tile fitting one wave.
+static bool pair_split(int64_t ntiles, int nst, int sms) { return nst % 2 == 0 && 2 * ntiles <= sms; }
+
+// The grid a call gets: two CTAs per tile (pair split) or one persistent CTA per SM.
+static int grid_for(int64_t ntiles, int nst, int sms) {
+  const int64_t units = ntiles * nst;
+  return pair_split(ntiles, nst, sms) ? (int)(2 * ntiles) : (int)(units < sms ? units : sms);
 }
 
 template <int SMODE, bool XBF16>
@@ -485,7 +620,8 @@ static int32_t launch_t(const LinearArgs &a, const Workspace &w, cudaStream_t st
   p.nst = (int)(a.cols / KS);
   p.ntiles = (int)((a.rows + TM - 1) / TM);
   p.units = (int64_t)p.ntiles * p.nst;
-  p.grid = (int)(p.units < sms ? p.units : sms);
+  p.pair = pair_split(p.ntiles, p.nst, sms) ? 1 : 0;
+  p.grid = grid_for(p.ntiles, p.nst, sms);
   p.m = (int)a.m;
   p.N = 8 * p.m;
   const Layout l = layout_for(p.units, p.grid, p.nst, p.N);
@@ -495,6 +631,7 @@ static int32_t launch_t(const LinearArgs &a, const Workspace &w, cudaStream_t st
   p.b_off = l.b_off;
   p.sfb_off = l.sfb_off;
   p.sfa_off = l.sfa_off;
+  p.pair_off = l.pair_off;
   p.bar_off = l.bar_off;
   p.width = l.width;
   p.sfa_col = l.sfa_col;
@@ -525,17 +662,26 @@ static int32_t launch_t(const LinearArgs &a, const Workspace &w, cudaStream_t st
   if (int32_t rc = make_tma_2d(&tmw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, row_bytes, (uint64_t)a.rows, row_bytes, 128, TM,
                                CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
-  B200_CUDA_TRY((ensure_dynamic_smem<mxs_kernel<SMODE, XBF16>>(210 * 1024)));
+  B200_CUDA_TRY((ensure_dynamic_smem<mxs_kernel<SMODE, XBF16>>(SMEM_MAX)));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.grid);
   cfg.blockDim = dim3(THREADS);
   cfg.dynamicSmemBytes = l.smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attrs[1];
-  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attrs[2];
+  unsigned nattr = 0;
+  if (a.flags & B200_FLAG_PDL) {
+    attrs[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[nattr++].val.programmaticStreamSerializationAllowed = 1;
+  }
+  if (p.pair) {
+    attrs[nattr].id = cudaLaunchAttributeClusterDimension;
+    attrs[nattr].val.clusterDim.x = 2;
+    attrs[nattr].val.clusterDim.y = 1;
+    attrs[nattr++].val.clusterDim.z = 1;
+  }
   cfg.attrs = attrs;
-  cfg.numAttrs = (a.flags & B200_FLAG_PDL) ? 1 : 0;
+  cfg.numAttrs = nattr;
   B200_CUDA_TRY(cudaLaunchKernelEx(&cfg, mxs_kernel<SMODE, XBF16>, tmw, p));
   return B200_OK;
 }
@@ -551,17 +697,20 @@ bool mxs_supported(const LinearArgs &a) {
   int sms = 0;
   if (device_sms(&sms) != cudaSuccess) return false;
   const int nst = (int)(a.cols / KS);
-  const int64_t units = ((a.rows + TM - 1) / TM) * (int64_t)nst;
-  const int grid = (int)(units < sms ? units : sms);
-  return layout_for(units, grid, nst, 8 * (int)a.m).stages != 0;
+  const int64_t ntiles = (a.rows + TM - 1) / TM;
+  const int64_t units = ntiles * (int64_t)nst;
+  return layout_for(units, grid_for(ntiles, nst, sms), nst, 8 * (int)a.m).stages != 0;
 }
 
 // Whether the automatic path should take this kernel over the mma.sync decode GEMV: only when
-// every CTA streams enough stages to amortise the fixed costs of a call (x conversion, scale
-// atoms, the split-tile fixup; about 4 us). Measured, FP4 E8M0 bf16, units per CTA in
-// brackets: 57344 x 8192 [97] M=1 45.6 vs 50.0 us, M=2 48.7 vs 62.1, M=4 76.3 vs 92.5;
-// 8192 x 28672 [48] M=1 29.6 vs 36.5, M=2 34.0 vs 114, M=4 48.3 vs 44.3; 10240 x 8192 [18]
-// M=1 16.6 vs 16.1; 8192 x 8192 [14] M=1 16.6 vs 10.7.
+// every CTA streams enough stages to amortise the fixed costs of a call (after the previous
+// kernel completes: the x load, queued behind the weight stream, and its conversion, ~2.5 us;
+// after the last unit: the epilogue and the pair or ticket reduction, ~2.5 us). Measured, FP4
+// E8M0 bf16, CUDA-graph replay with PDL, stream-K units per CTA in brackets, this kernel vs
+// the mma.sync kernels: 57344 x 8192 [97] M=1 46.9 vs 49.5 us, M=2 49.1 vs 62.1, M=4 55.4 vs
+// 92.5; 8192 x 28672 [48, pair split] M=1 31.2 vs 36.4, M=2 34.3 vs 114.6, M=4 48.3 vs 44.1;
+// 10240 x 8192 [18] M=1 18.0 vs 16.1; 8192 x 8192 [14, pair split] M=1 13.0 vs 10.6, M=2 15.1
+// vs 13.1; 7168 x 8192 [pair split] M=1 12.6 vs 10.1.
 bool mx_preferred(const LinearArgs &a) {
   using namespace mxs;
   if (!mxs_supported(a)) return false;
