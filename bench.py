@@ -175,6 +175,7 @@ def run_gpu_arm(args, world, rank, local):
     y = torch.empty((cfg["m"], cfg["n"]), device=device, dtype=xdt)
     plan = linear_plan(ws[0], xdt, cfg["m"], xdt)
     descs = [w.desc() for w in ws]
+    sflags = [w.scale_flags() for w in ws]  # B200_FLAG_SCALES_ORDINARY, as tg.matmul passes it
     fn = _lib.lib().b200_packed_linear
     xdt_code, ydt_code = _lib.DT[cfg["xdt"]], _lib.DT[cfg["xdt"]]
 
@@ -184,7 +185,7 @@ def run_gpu_arm(args, world, rank, local):
 
     def launch(i, stream):
         rc = fn(ctypes.byref(descs[i % copies]), x.data_ptr(), xdt_code, cfg["m"], cfg["k"], 1, y.data_ptr(),
-                ydt_code, cfg["n"], 1, pdl, stream)
+                ydt_code, cfg["n"], 1, pdl | sflags[i % copies], stream)
         if rc:
             raise RuntimeError(_lib.last_error())
 
@@ -399,12 +400,13 @@ def run_configs(args, device, world, rank):
         x = torch.randn((cfg["m"], cfg["k"]), device=device).to(xdt)
         y = torch.empty((cfg["m"], cfg["n"]), device=device, dtype=xdt)
         descs = [w.desc() for w in ws]
+        sflags = [w.scale_flags() for w in ws]
         code = _lib.DT[cfg["xdt"]]
         flags = 0x100  # B200_FLAG_PDL (the decode kernels at these token counts honour it)
 
         def launch(i, stream):
             rc = fn(ctypes.byref(descs[i % copies]), x.data_ptr(), code, cfg["m"], cfg["k"], 1, y.data_ptr(), code,
-                    cfg["n"], 1, flags, stream)
+                    cfg["n"], 1, flags | sflags[i % copies], stream)
             if rc:
                 raise RuntimeError(_lib.last_error())
 
@@ -435,8 +437,8 @@ def run_configs(args, device, world, rank):
 
     def launch5(i, stream):
         for k, w in ws5.items():
-            rc = fn(ctypes.byref(d5[k]), xs[k].data_ptr(), bf, m5, w.shape[1], 1, ys[k].data_ptr(), bf, w.shape[0], 1, 0,
-                    stream)
+            rc = fn(ctypes.byref(d5[k]), xs[k].data_ptr(), bf, m5, w.shape[1], 1, ys[k].data_ptr(), bf, w.shape[0], 1,
+                    w.scale_flags(), stream)
             if rc:
                 raise RuntimeError(_lib.last_error())
 
@@ -504,11 +506,12 @@ def run_strong(args, device, world, rank):
         x = torch.randn((1, cfg["k"]), device=device).to(xdt)
         y = torch.empty((1, cfg["n"]), device=device, dtype=xdt)
         descs = [w.desc() for w in ws]
+        sflags = [w.scale_flags() for w in ws]
         code = _lib.DT[cfg["xdt"]]
 
         def launch(i, stream):
             rc = fn(ctypes.byref(descs[i % copies]), x.data_ptr(), code, 1, cfg["k"], 1, y.data_ptr(), code, cfg["n"], 1,
-                    0x100, stream)
+                    0x100 | sflags[i % copies], stream)
             if rc:
                 raise RuntimeError(_lib.last_error())
 
@@ -837,7 +840,8 @@ def profile_case(case: str, launches: int):
     fn = _lib.lib().b200_packed_linear
     for i in range(launches):
         d = ws[i % len(ws)].desc()
-        rc = fn(ctypes.byref(d), x.data_ptr(), code, cfg["m"], cfg["k"], 1, y.data_ptr(), code, cfg["n"], 1, 0, None)
+        rc = fn(ctypes.byref(d), x.data_ptr(), code, cfg["m"], cfg["k"], 1, y.data_ptr(), code, cfg["n"], 1,
+                ws[i % len(ws)].scale_flags(), None)
         if rc:
             raise RuntimeError(_lib.last_error())
     torch.cuda.synchronize()

@@ -152,9 +152,10 @@ def test_public_api_call_forms():
 
 @pytest.mark.parametrize("m", [1, 2])
 def test_e8m0_special_bytes(m):
-    """E8M0 byte 0 (2^-127, an fp32 subnormal) and extreme exponents next to ordinary ones:
-    the decode GEMV converts bytes 1..254 with a shift and must take the exact conversion
-    for byte 0. Row 0 is scaled by 2^-127 everywhere and is compared after rescaling."""
+    """E8M0 byte 0 (2^-127, an fp32 subnormal), byte 255 (NaN) and extreme exponents next to
+    ordinary ones: the decode GEMV converts bytes 1..254 with a shift and must take the exact
+    conversion for bytes 0 and 255. Row 0 is scaled by 2^-127 everywhere and is compared after
+    rescaling; row 3 has one NaN block scale, so its outputs are NaN."""
     from tinygrad_dx12_b200.linalg import _packed_linear
 
     rng = np.random.default_rng(21)
@@ -166,11 +167,14 @@ def test_e8m0_special_bytes(m):
     spec = ref.PackedSpec(base.data, base.format, base.shape, np.exp2(e.astype(np.float64)).astype(np.float32), 32,
                           "float32")
     w = to_device(spec, DEV, "e8m0")
+    w.scales.view(torch.uint8)[3, 5] = 255
     x = torch.from_numpy(rng.standard_normal((m, 2048)).astype(np.float32)).to(DEV).to(torch.bfloat16)
     y = _packed_linear(w, x, torch.float32, "gemv").cpu().numpy()
     wf = ref.dequant(spec.data, spec.format, spec.shape, spec.scales, 32, "float32", "float32")
     r = x.float().cpu().numpy() @ wf.T
-    assert_close(y[:, 1:], r[:, 1:], "float32")
+    assert np.isnan(y[:, 3]).all()
+    keep = np.arange(256) != 3
+    assert_close(y[:, 1:][:, keep[1:]], r[:, 1:][:, keep[1:]], "float32")
     y0, r0 = y[:, 0].astype(np.float64) * 2.0**127, r[:, 0].astype(np.float64) * 2.0**127
     assert np.all(np.abs(y0 - r0) <= 1e-3 * np.maximum(np.abs(r0), 1.0))
 

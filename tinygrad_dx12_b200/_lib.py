@@ -27,6 +27,8 @@ DT = {
 }
 PATH = {"auto": 0, "gemv": 1, "gemm": 2, "simt": 3, "mx": 4}
 PATH_NAME = {v: k for k, v in PATH.items()}
+FLAG_PDL = 0x100               # B200_FLAG_PDL
+FLAG_SCALES_ORDINARY = 0x200   # B200_FLAG_SCALES_ORDINARY
 
 
 class PackedDesc(ctypes.Structure):

@@ -105,8 +105,37 @@ struct Chunk4 {
   Chunk<BITS> lo, hi;  // rows g, g+8 | rows g+16, g+24
 };
 
+// E8M0 bytes -> float32 scales, four per word (byte i -> out[i]). Bytes 1..254 are 2^(b-127) =
+// float bits b << 23; bytes 0 (2^-127, subnormal) and 255 (NaN) take the exact conversion, a
+// warp-uniform branch that ordinary scales never take. The zero-byte test of v and of ~v
+// ((v - 0x01..) & ~v & 0x80..) finds both without per-byte compares.
+// With `ordinary` (the caller's B200_FLAG_SCALES_ORDINARY: no byte 0 or 255 in the matrix) the
+// test is skipped.
+__device__ __forceinline__ void e8m0_scales8(uint32_t v01, uint32_t v23, float (&lo)[4], float (&hi)[4],
+                                             bool ordinary) {
+  constexpr uint32_t K1 = 0x01010101u, H = 0x80808080u;
+  bool exact = false;
+  if (!ordinary) {  // kernel parameter: uniform
+    const uint32_t sp = (((v01 - K1) & ~v01) | ((~v01 - K1) & v01) | ((v23 - K1) & ~v23) | ((~v23 - K1) & v23)) & H;
+    exact = __any_sync(0xffffffffu, sp != 0u);
+  }
+  if (exact) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) lo[i] = e8m0_fast((v01 >> (8 * i)) & 0xFFu), hi[i] = e8m0_fast((v23 >> (8 * i)) & 0xFFu);
+  } else {
+    lo[0] = __uint_as_float((v01 & 0xFFu) << 23), lo[1] = __uint_as_float((v01 & 0xFF00u) << 15);
+    lo[2] = __uint_as_float((v01 & 0xFF0000u) << 7), lo[3] = __uint_as_float((v01 & 0xFF000000u) >> 1);
+    hi[0] = __uint_as_float((v23 & 0xFFu) << 23), hi[1] = __uint_as_float((v23 & 0xFF00u) << 15);
+    hi[2] = __uint_as_float((v23 & 0xFF0000u) << 7), hi[3] = __uint_as_float((v23 & 0xFF000000u) >> 1);
+  }
+}
+
+// The MMAs of one chunk, then its per-block scales: for E8M0, `e01` / `e23` hold the raw scale
+// bytes (rows g, g+8 | g+16, g+24; blocks blk, blk+1 of each) and are converted after the MMAs
+// are issued, so the conversion fills the MMA latency instead of preceding it.
 template <int FMT, int SK>
-__device__ __forceinline__ void compute_chunk4(const Chunk4<Fmt<FMT>::bits> &r, const __half *xblk, float (&acc)[4]) {
+__device__ __forceinline__ void compute_chunk4(const Chunk4<Fmt<FMT>::bits> &r, const __half *xblk, float (&acc)[4],
+                                               uint32_t e01 = 0u, uint32_t e23 = 0u, bool ordinary = false) {
   constexpr int BITS = Fmt<FMT>::bits;
   float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -138,6 +167,13 @@ __device__ __forceinline__ void compute_chunk4(const Chunk4<Fmt<FMT>::bits> &r, 
     acc[1] += d0[2] + d0[3];
     acc[2] += d1[0] + d1[1];
     acc[3] += d1[2] + d1[3];
+  } else if constexpr (SK == SK_E8M0) {
+    float lo[4], hi[4];
+    e8m0_scales8(e01, e23, lo, hi, ordinary);
+    acc[0] = fmaf(d0[0], lo[0], fmaf(d0[1], lo[1], acc[0]));
+    acc[1] = fmaf(d0[2], lo[2], fmaf(d0[3], lo[3], acc[1]));
+    acc[2] = fmaf(d1[0], hi[0], fmaf(d1[1], hi[1], acc[2]));
+    acc[3] = fmaf(d1[2], hi[2], fmaf(d1[3], hi[3], acc[3]));
   } else {
     acc[0] = fmaf(d0[0], r.lo.sa0, fmaf(d0[1], r.lo.sa1, acc[0]));
     acc[1] = fmaf(d0[2], r.lo.sb0, fmaf(d0[3], r.lo.sb1, acc[1]));
@@ -170,6 +206,7 @@ struct StreamParams {
   int64_t nrb;  // row blocks
   int nst;      // stages per row block
   int xbf16;
+  int ordinary;  // B200_FLAG_SCALES_ORDINARY: E8M0 scale bytes known to lie in 1..254
   // Staged scales: gshift = log2(block / 32) (0: one scale per 32-payload block; 1..4: group
   // scales of 64..512 payloads). Each stage loads a box of sbe scales per row that starts at a
   // multiple of sbe, since a TMA box is at least 16 bytes wide (four fp16 group-128 scales
@@ -340,32 +377,18 @@ __global__ void __launch_bounds__(threads<NC>(), 1)
       const bool got = mbar_wait(&full[slot], round, abort_flag);
       const uint8_t *base = ring + slot * SLOT;
       Chunk4<BITS> r;
+      uint32_t e01 = 0u, e23 = 0u;  // E8M0: raw scale bytes, converted after the chunk's MMAs
       if (got) {
         read_rows<BITS>(r.lo, base, g, g + 8, sub, t);
         read_rows<BITS>(r.hi, base, g + 16, g + 24, sub, t);
         if constexpr (SK == SK_E8M0) {
-          // E8M0 bytes 1..254 are 2^(b-127) = float bits b << 23; bytes 0 (2^-127, subnormal)
-          // and 255 (NaN) take the exact conversion (warp-uniform branch, rare)
           const uint8_t *sb = base + RB * WR;
           const int blk = sub * 4 + cblk;
           const uint32_t u0 = *reinterpret_cast<const uint16_t *>(sb + (g * (KSTAGE / 32) + blk));
           const uint32_t u1 = *reinterpret_cast<const uint16_t *>(sb + ((g + 8) * (KSTAGE / 32) + blk));
           const uint32_t u2 = *reinterpret_cast<const uint16_t *>(sb + ((g + 16) * (KSTAGE / 32) + blk));
           const uint32_t u3 = *reinterpret_cast<const uint16_t *>(sb + ((g + 24) * (KSTAGE / 32) + blk));
-          const uint32_t v01 = u0 | (u1 << 16), v23 = u2 | (u3 << 16);
-          const uint32_t special = __vcmpeq4(v01, 0u) | __vcmpeq4(v23, 0u) | __vcmpeq4(v01, 0xFFFFFFFFu) |
-                                   __vcmpeq4(v23, 0xFFFFFFFFu);
-          if (__any_sync(0xffffffffu, special != 0u)) {
-            r.lo.sa0 = e8m0_fast(u0 & 0xFFu), r.lo.sa1 = e8m0_fast(u0 >> 8);
-            r.lo.sb0 = e8m0_fast(u1 & 0xFFu), r.lo.sb1 = e8m0_fast(u1 >> 8);
-            r.hi.sa0 = e8m0_fast(u2 & 0xFFu), r.hi.sa1 = e8m0_fast(u2 >> 8);
-            r.hi.sb0 = e8m0_fast(u3 & 0xFFu), r.hi.sb1 = e8m0_fast(u3 >> 8);
-          } else {
-            r.lo.sa0 = __uint_as_float((u0 & 0xFFu) << 23), r.lo.sa1 = __uint_as_float((u0 & 0xFF00u) << 15);
-            r.lo.sb0 = __uint_as_float((u1 & 0xFFu) << 23), r.lo.sb1 = __uint_as_float((u1 & 0xFF00u) << 15);
-            r.hi.sa0 = __uint_as_float((u2 & 0xFFu) << 23), r.hi.sa1 = __uint_as_float((u2 & 0xFF00u) << 15);
-            r.hi.sb0 = __uint_as_float((u3 & 0xFFu) << 23), r.hi.sb1 = __uint_as_float((u3 & 0xFF00u) << 15);
-          }
+          e01 = u0 | (u1 << 16), e23 = u2 | (u3 << 16);
         } else if constexpr (GROUP) {
           const uint8_t *sb = base + RB * WR;
           const int blk = sub * 4 + cblk;  // block index within the stage's 16 blocks per row (even)
@@ -387,7 +410,7 @@ __global__ void __launch_bounds__(threads<NC>(), 1)
       if (lane == 0) mbar_arrive(&empty[slot]);  // the slot's data now lives in registers
       if (got) {
         const int chunk = st * CPS + sub;
-        compute_chunk4<FMT, SK>(r, owner ? xrow + (int64_t)chunk * CHUNK : zslot, acc);
+        compute_chunk4<FMT, SK>(r, owner ? xrow + (int64_t)chunk * CHUNK : zslot, acc, e01, e23, sp.ordinary != 0);
       }
     }
     // ---- reduce this row block over the NC consumer warps and store ----
@@ -463,6 +486,7 @@ static int32_t launch_t(const LinearArgs &a, cudaStream_t stream) {
   sp.nrb = (a.rows + RB - 1) / RB;
   sp.nst = (int)(a.cols / KSTAGE);
   sp.xbf16 = a.xdt == B200_DT_BF16;
+  sp.ordinary = (a.flags & B200_FLAG_SCALES_ORDINARY) != 0;
   sp.gshift = gshift;
   sp.sbe = sbe;
   sp.tx = (uint32_t)(RB * wrow<BITS>() + RB * sbe * SESZ);

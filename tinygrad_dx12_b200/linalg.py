@@ -138,8 +138,8 @@ def _packed_linear(w: PackedTensor, x: torch.Tensor, out_dtype: torch.dtype, pat
         y = torch.empty((m, w.rows), device=x.device, dtype=out_dtype)
     d = w.desc()
     _lib.call("b200_packed_linear", ctypes_ref(d), x.data_ptr(), _lib.DT[D.name(x.dtype)], m, ldx, 1,
-              y.data_ptr(), _lib.DT[D.name(out_dtype)], y.stride(0) if m > 1 else w.rows, 1, _lib.PATH[path] | flags,
-              stream_ptr(x.device))
+              y.data_ptr(), _lib.DT[D.name(out_dtype)], y.stride(0) if m > 1 else w.rows, 1,
+              _lib.PATH[path] | flags | w.scale_flags(), stream_ptr(x.device))
     return y
 
 
@@ -152,7 +152,7 @@ def _packed_linear_multi(w: PackedTensor, x: torch.Tensor, y_ptrs, out_dtype: to
     ldx = x.stride(0) if m > 1 else -(-x.shape[1] // 8) * 8
     d = w.desc()
     _lib.call("b200_packed_linear_multi", ctypes_ref(d), x.data_ptr(), _lib.DT[D.name(x.dtype)], m, ldx, y_ptrs,
-              len(y_ptrs), _lib.DT[D.name(out_dtype)], ldy, flags, stream_ptr(x.device))
+              len(y_ptrs), _lib.DT[D.name(out_dtype)], ldy, flags | w.scale_flags(), stream_ptr(x.device))
 
 
 def linear_plan(w: PackedTensor, x_dtype: torch.dtype, m: int, out_dtype: torch.dtype, path: str = "auto") -> str | None:
@@ -297,7 +297,7 @@ def _host_decode_step(a: PackedTensor, b: torch.Tensor, dtype, out):
     _lib.call("b200_cast", b.data_ptr(), xcode, buf.data_ptr(), xcode, m * kdim, stream)
     y = torch.empty((m, n), device=device, dtype=dtype) if out is None else out
     _lib.call("b200_packed_linear", ctypes_ref(a.desc()), buf.data_ptr(), xcode, m, kdim, 1, y.data_ptr(), ycode, n,
-              1, _lib.PATH[path], stream)
+              1, _lib.PATH[path] | a.scale_flags(), stream)
     if _profile_hook is not None:
         _report(path, a, b, dtype)
     return out if out is not None else y.t()

@@ -98,6 +98,27 @@ class PackedTensor:
     def cols(self) -> int:
         return self.shape[-1]
 
+    def scale_flags(self) -> int:
+        """``B200_FLAG_SCALES_ORDINARY`` when the scales are E8M0 and none is byte 0x00 (2^-127) or
+        0xFF (NaN), else 0. Checked once per tensor (one reduction on the device, one read back)
+        and cached: after writing such a byte into ``scales`` in place, call
+        ``refresh_scale_flags()``."""
+        cached = self.__dict__.get("_sflags")
+        if cached is not None:
+            return cached
+        f = 0
+        s = self.scales
+        if s is not None and s.dtype == torch.float8_e8m0fnu and s.device.type == "cuda":
+            b = s.view(torch.uint8)
+            if b.numel() == 0 or not bool(((b == 0) | (b == 255)).any()):
+                f = _lib.FLAG_SCALES_ORDINARY
+        object.__setattr__(self, "_sflags", f)
+        return f
+
+    def refresh_scale_flags(self) -> None:
+        """Forget the cached scale check (see ``scale_flags``)."""
+        self.__dict__.pop("_sflags", None)
+
     def desc(self) -> _lib.PackedDesc:
         """The C-ABI descriptor (rows = prod(shape[:-1]), cols = shape[-1]).
 
