@@ -83,8 +83,27 @@ __global__ void cast_kernel(const void *src, int sdt, void *dst, int ddt, int64_
   }
 }
 
+// Same-dtype copy in 16-byte vectors (the staging copy of a decode step's activations from
+// pinned host memory: one load per thread over the host link). It lets a dependent kernel
+// launched with programmatic dependent launch start at once (that kernel streams its weights
+// while this copy runs and waits for it before reading the copy).
+__global__ void copy16_kernel(const uint4 *src, uint4 *dst, int64_t n16) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+
 int32_t launch_cast(const void *src, int sdt, void *dst, int ddt, int64_t n, cudaStream_t stream) {
   if (n <= 0) return B200_OK;
+  const int64_t bytes = n * dt_size(sdt);
+  if (sdt == ddt && bytes % 16 == 0 && (uintptr_t)src % 16 == 0 && (uintptr_t)dst % 16 == 0) {
+    const int64_t n16 = bytes / 16;
+    int64_t blocks = (n16 + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    copy16_kernel<<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const uint4 *>(src), static_cast<uint4 *>(dst), n16);
+    B200_LAUNCH_CHECK();
+    return B200_OK;
+  }
   int64_t blocks = (n + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   cast_kernel<<<(unsigned)blocks, 256, 0, stream>>>(src, sdt, dst, ddt, n);

@@ -12,6 +12,7 @@ as one graph launch instead of one host call each.
 
 from __future__ import annotations
 
+import ctypes
 import time
 
 import torch
@@ -36,11 +37,14 @@ class GraphStep:
             if t.device.type == "cpu":
                 if not t.is_pinned():
                     raise ValueError("host inputs of a graph step must be in pinned memory")
-                s = torch.empty_like(t).pin_memory()
+                s = torch.empty_like(t, memory_format=torch.contiguous_format).pin_memory()
                 s.copy_(t)
             else:
                 s = t.clone()
             self.static.append(s)
+        # per input: (static buffer, is host, bytes) -- a host input is copied with one memmove
+        self._slots = [(s, s.device.type == "cpu", s.numel() * s.element_size()) for s in self.static]
+        self._host = any(h for _, h, _ in self._slots)
         self.device = next((t.device for t in inputs if t.device.type == "cuda"), torch.device("cuda", torch.cuda.current_device()))
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
@@ -57,23 +61,35 @@ class GraphStep:
         self._done.record(torch.cuda.current_stream(self.device))
 
     def __call__(self, *inputs: torch.Tensor, wait: bool = False):
-        if len(inputs) not in (0, len(self.static)):
-            raise ValueError(f"GraphStep takes {len(self.static)} inputs")
-        stream = torch.cuda.current_stream(self.device)
-        for new, s in zip(inputs, self.static):
-            if new is s or (new.data_ptr() == s.data_ptr() and new.shape == s.shape):
+        if len(inputs) not in (0, len(self._slots)):
+            raise ValueError(f"GraphStep takes {len(self._slots)} inputs")
+        waited = False
+        for new, (s, host, nbytes) in zip(inputs, self._slots):
+            if new is s:
                 continue
             if new.shape != s.shape or new.dtype != s.dtype:
                 raise ValueError(f"input of shape {tuple(new.shape)} {new.dtype}, recorded {tuple(s.shape)} {s.dtype}")
-            if s.device.type == "cpu":
-                self._done.synchronize()  # the previous replay's staging copy has read the old host input
-                s.copy_(new)
+            if host:
+                if new.device.type != "cpu" or not new.is_contiguous():
+                    raise ValueError("a host input of a graph step must be a contiguous host tensor")
+                if not waited:  # the previous replay's staging copy has read the old host inputs
+                    self._done.synchronize()
+                    waited = True
+                ctypes.memmove(s.data_ptr(), new.data_ptr(), nbytes)
             else:
                 s.copy_(new, non_blocking=True)
+        if torch.cuda.current_device() != self.device.index:
+            with torch.cuda.device(self.device):
+                return self._replay(wait)
+        return self._replay(wait)
+
+    def _replay(self, wait: bool):
         if not wait:
             self.graph.replay()
-            self._done.record(stream)
+            if self._host:
+                self._done.record()  # this device's current stream
             return self.outputs
+        stream = torch.cuda.current_stream(self.device)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record(stream)
         self.graph.replay()

@@ -296,8 +296,10 @@ def _host_decode_step(a: PackedTensor, b: torch.Tensor, dtype, out):
     xcode, ycode = _lib.DT[D.name(b.dtype)], _lib.DT[D.name(dtype)]
     _lib.call("b200_cast", b.data_ptr(), xcode, buf.data_ptr(), xcode, m * kdim, stream)
     y = torch.empty((m, n), device=device, dtype=dtype) if out is None else out
+    # B200_FLAG_PDL: the decode kernel streams its weights while the staging copy runs, and waits
+    # for the copy before reading x
     _lib.call("b200_packed_linear", ctypes_ref(a.desc()), buf.data_ptr(), xcode, m, kdim, 1, y.data_ptr(), ycode, n,
-              1, _lib.PATH[path] | a.scale_flags(), stream)
+              1, _lib.PATH[path] | a.scale_flags() | _lib.FLAG_PDL, stream)
     if _profile_hook is not None:
         _report(path, a, b, dtype)
     return out if out is not None else y.t()
