@@ -67,7 +67,7 @@ constexpr int TMEM_THREADS = PROD_WARP0 * 32;  // every warp but the producers
 constexpr int STAGE_BYTES = TM * 128;          // 128 rows x 256 FP4 codes
 constexpr int SFR = 8;                         // scale-factor atom ring (units in flight)
 constexpr int MAX_M = 4;
-constexpr int MAX_STAGES = 12;
+constexpr int MAX_STAGES = 8;
 constexpr int SMEM_MAX = 227 * 1024;            // dynamic shared memory a CTA may take
 
 struct Params {
@@ -286,33 +286,25 @@ __global__ void __launch_bounds__(THREADS, 1) mxs_kernel(const __grid_constant__
         if (s >= nst) s -= nst;  // b < nst
         raw[q] = *reinterpret_cast<const uint4 *>(p.x + (int64_t)mm * p.ldx + (int64_t)s * KS + 8 * lane);
       }
-      // the four pairs' pieces are computed before any is stored, so their dependency chains
-      // (eight pieces each) overlap; the conversion is on the path to the first MMA
-      uint32_t pc[4][8], byte0[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (q0 + q < pairs) {  // warp-uniform
-          float v[8];
-          raw_to_f32<XBF16>(raw[q], v);
-          byte0[q] = split_fp4<8>(v, pc[q]);
-        }
-      }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         if (q0 + q >= pairs) break;
         const int b = cw + 8 * ((q0 + q) / p.m), mm = (q0 + q) % p.m;
+        float v[8];
+        raw_to_f32<XBF16>(raw[q], v);
+        uint32_t pc[8];
+        const uint32_t byte0 = split_fp4<8>(v, pc);
         uint8_t *bt = bres + (size_t)b * p.N * 128;
         uint8_t *atom = sfb_atoms + (size_t)b * sfbs + (kb < 4 ? kb : 4 + kb);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const uint32_t j = (uint32_t)(mm * 8 + c);  // B row of token mm's piece c
-          *reinterpret_cast<uint32_t *>(bt + j * 128 + ((chunk ^ (j & 7)) << 4) + off) = pc[q][c];
-          if ((lane & 3) == 0)
-            atom[j * 16] = (uint8_t)(byte0[q] == 255u ? (c == 0 ? 255u : 127u) : byte0[q] - 2u * c);
+          *reinterpret_cast<uint32_t *>(bt + j * 128 + ((chunk ^ (j & 7)) << 4) + off) = pc[c];
+          if ((lane & 3) == 0) atom[j * 16] = (uint8_t)(byte0 == 255u ? (c == 0 ? 255u : 127u) : byte0 - 2u * c);
         }
-        if (mm == p.m - 1) {  // the slot's last token: its pieces and scales are ready
-          fence_proxy_async_smem();
-          __syncwarp();
+        if (mm == p.m - 1) {  // the slot's last token: its pieces and scales are ready (publishing
+          fence_proxy_async_smem();  // each slot at once measured faster than converting four
+          __syncwarp();              // slots' pieces together and publishing them after)
           if (lane == 0) mbar_arrive(&bready[b]);
         }
       }
@@ -707,10 +699,10 @@ bool mxs_supported(const LinearArgs &a) {
 // kernel completes: the x load, queued behind the weight stream, and its conversion, ~2.5 us;
 // after the last unit: the epilogue and the pair or ticket reduction, ~2.5 us). Measured, FP4
 // E8M0 bf16, CUDA-graph replay with PDL, stream-K units per CTA in brackets, this kernel vs
-// the mma.sync kernels: 57344 x 8192 [97] M=1 46.9 vs 49.5 us, M=2 49.1 vs 62.1, M=4 55.4 vs
-// 92.5; 8192 x 28672 [48, pair split] M=1 31.2 vs 36.4, M=2 34.3 vs 114.6, M=4 48.3 vs 44.1;
-// 10240 x 8192 [18] M=1 18.0 vs 16.1; 8192 x 8192 [14, pair split] M=1 13.0 vs 10.6, M=2 15.1
-// vs 13.1; 7168 x 8192 [pair split] M=1 12.6 vs 10.1.
+// the mma.sync kernels: 57344 x 8192 [97] M=1 45.6 vs 49.0 us, M=2 48.8 vs 61.1, M=4 56.3 vs
+// 92.6; 8192 x 28672 [48, pair split] M=1 30.2 vs 36.2, M=2 33.8 vs 114.4, M=4 48.2 vs 44.1;
+// 10240 x 8192 [18] M=1 16.7 vs 15.8; 8192 x 8192 [14, pair split] M=1 12.4 vs 10.6, M=2 14.3
+// vs 13.1; 7168 x 8192 [pair split] M=1 12.1 vs 10.1.
 bool mx_preferred(const LinearArgs &a) {
   using namespace mxs;
   if (!mxs_supported(a)) return false;
