@@ -89,7 +89,8 @@ extern "C" {
 #define B200_FLAG_PDL 0x100
 /* OR-able flag: the caller guarantees that no E8M0 scale byte of the matrix is 0x00 (2^-127)
  * or 0xFF (NaN). The decode GEMV then converts every byte with a shift and skips its per-stage
- * test for those two bytes (about 5 % of a one-token call). Results with such a byte present
+ * test for those two bytes (about 5 % of a one-token call), and the decode GEMM for 3..64
+ * tokens runs its shift-only instantiation (about 9 % at 8 tokens). Results with such a byte present
  * and the flag set are undefined; without the flag every byte is decoded exactly. The Python
  * layer sets it per weight after checking the scales once. Ignored for other scale types. */
 #define B200_FLAG_SCALES_ORDINARY 0x200

@@ -150,11 +150,11 @@ def test_public_api_call_forms():
     assert_close(yc.t().float().cpu().numpy(), r, "float16")
 
 
-@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("m", [1, 2, 8])
 def test_e8m0_special_bytes(m):
     """E8M0 byte 0 (2^-127, an fp32 subnormal), byte 255 (NaN) and extreme exponents next to
-    ordinary ones: the decode GEMV converts bytes 1..254 with a shift and must take the exact
-    conversion for bytes 0 and 255. Row 0 is scaled by 2^-127 everywhere and is compared after
+    ordinary ones: the decode kernels (one or two tokens; eight) convert bytes 1..254 with a shift
+    and must take the exact conversion for bytes 0 and 255. Row 0 is scaled by 2^-127 everywhere and is compared after
     rescaling; row 3 has one NaN block scale, so its outputs are NaN."""
     from tinygrad_dx12_b200.linalg import _packed_linear
 

@@ -90,10 +90,17 @@ __host__ __device__ constexpr int stages(int esz) {
 // (stage * groups per stage) mod box. SK_GROUP reads group scales from global memory instead
 // (other shapes: E8M0 groups, scale rows that are not 16-byte multiples, fp32 group-64).
 constexpr int SK_GSTAGED = 16;
+// Per-32 E8M0 scales under B200_FLAG_SCALES_ORDINARY (no byte 0 or 255 in the matrix): the same
+// kernel with 2^(b-127) taken as float bits b << 23, one shift instead of the exact conversion.
+constexpr int SK_E8M0_ORD = 17;
+template <int SK>
+__host__ __device__ constexpr bool is_e8m0() {
+  return SK == gemv::SK_E8M0 || SK == SK_E8M0_ORD;
+}
 
 template <int SK>
 __host__ __device__ constexpr int tile_esz() {  // staged scale bytes per 32-payload block and row
-  return SK == SK_E8M0 || SK == SK_GSTAGED ? 1 : SK == SK_F16 || SK == SK_BF16 ? 2 : SK == SK_F32 ? 4 : 0;
+  return is_e8m0<SK>() || SK == SK_GSTAGED ? 1 : SK == SK_F16 || SK == SK_BF16 ? 2 : SK == SK_F32 ? 4 : 0;
 }
 
 struct SkParams {
@@ -123,7 +130,8 @@ __device__ __forceinline__ float e8m0_val(uint32_t b) {
 
 template <int SK>
 __device__ __forceinline__ float tile_scale(const uint8_t *srow, int b) {
-  if constexpr (SK == SK_E8M0) return e8m0_val(srow[b]);
+  if constexpr (SK == SK_E8M0_ORD) return __uint_as_float((uint32_t)srow[b] << 23);
+  else if constexpr (SK == SK_E8M0) return e8m0_val(srow[b]);
   else if constexpr (SK == SK_F16) return __half2float(reinterpret_cast<const __half *>(srow)[b]);
   else if constexpr (SK == SK_BF16) return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(srow)[b] << 16);
   else if constexpr (SK == SK_F32) return reinterpret_cast<const float *>(srow)[b];
@@ -328,8 +336,8 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
       // the E8M0 scales of this warp's NB blocks, rows g / g+8 (word i holds local blocks 4i..4i+3)
       // (applied to each block's fp32 MMA result: folding them into the fp16 operand with HMUL2
       // measured slower on every tile, FP4 8192^2 M=8 20.98 vs 20.03 us, M=32 fp16 x 32.7 vs 29.5)
-      uint32_t e8l[SK == SK_E8M0 ? NB / 4 : 1] = {}, e8h[SK == SK_E8M0 ? NB / 4 : 1] = {};
-      if constexpr (SK == SK_E8M0) {
+      uint32_t e8l[is_e8m0<SK>() ? NB / 4 : 1] = {}, e8h[is_e8m0<SK>() ? NB / 4 : 1] = {};
+      if constexpr (is_e8m0<SK>()) {
         if constexpr (NB == 16) {
           const uint4 ul = *reinterpret_cast<const uint4 *>(srow_lo), uh = *reinterpret_cast<const uint4 *>(srow_hi);
           e8l[0] = ul.x, e8l[1] = ul.y, e8l[2] = ul.z, e8l[3] = ul.w;
@@ -358,11 +366,16 @@ __global__ void __launch_bounds__(threads<NT, SK>(), ctas_per_sm<NT>())
           decode8_natural<FMT, false>(&wh, 0, oh);
           const int xbox = bb >> 1;
           float sl = 1.f, sh = 1.f;
-          if constexpr (SK == SK_E8M0) {
+          if constexpr (is_e8m0<SK>()) {
             const int jb = 2 * jp + h;  // local block: compile-time word and byte
             const uint32_t bl = (e8l[jb >> 2] >> (8 * (jb & 3))) & 0xFFu, bh = (e8h[jb >> 2] >> (8 * (jb & 3))) & 0xFFu;
-            sl = e8m0_val(bl);
-            sh = e8m0_val(bh);
+            if constexpr (SK == SK_E8M0_ORD) {
+              sl = __uint_as_float(bl << 23);
+              sh = __uint_as_float(bh << 23);
+            } else {
+              sl = e8m0_val(bl);
+              sh = e8m0_val(bh);
+            }
           } else if constexpr (TILE_SCALES) {
             sl = tile_scale<SK>(srow_lo, bb);
             sh = tile_scale<SK>(srow_hi, bb);
@@ -617,7 +630,9 @@ static int32_t launch_sk(const LinearArgs &a, int sk, int splits, float *ws, uns
   switch (sk) {
     case SK_NONE: return launch_x<FMT, NT, SK_NONE>(a, splits, ws, tk, s);
     case SK_ROW: return launch_x<FMT, NT, SK_ROW>(a, splits, ws, tk, s);
-    case SK_E8M0: return launch_x<FMT, NT, SK_E8M0>(a, splits, ws, tk, s);
+    case SK_E8M0:
+      return (a.flags & B200_FLAG_SCALES_ORDINARY) ? launch_x<FMT, NT, SK_E8M0_ORD>(a, splits, ws, tk, s)
+                                                   : launch_x<FMT, NT, SK_E8M0>(a, splits, ws, tk, s);
     case SK_F16: return launch_x<FMT, NT, SK_F16>(a, splits, ws, tk, s);
     case SK_BF16: return launch_x<FMT, NT, SK_BF16>(a, splits, ws, tk, s);
     case SK_F32: return launch_x<FMT, NT, SK_F32>(a, splits, ws, tk, s);
