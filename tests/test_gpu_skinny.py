@@ -103,6 +103,25 @@ def test_repeated_calls_reuse_workspace():
         assert torch.equal(y, ys[0])
 
 
+def test_first_call_on_side_stream():
+    """The first split-K call on a new (non-blocking) torch stream creates that stream's
+    workspace and clears its tickets on the same stream, so it is ordered before the kernel."""
+    from tinygrad_dx12_b200.linalg import _packed_linear
+
+    spec = _case("fp4_e2m1", 1024, 4096, 32, "e8m0", seed=4)
+    w = to_device(spec, DEV, "e8m0")
+    x = torch.randn((8, 4096), device=DEV).to(torch.bfloat16)
+    want = _packed_linear(w, x, torch.float32, "gemv")
+    torch.cuda.synchronize()
+    for _ in range(3):
+        side = torch.cuda.Stream(DEV)
+        side.wait_stream(torch.cuda.current_stream(DEV))
+        with torch.cuda.stream(side):
+            got = _packed_linear(w, x, torch.float32, "gemv")
+        side.synchronize()
+        assert torch.equal(got, want)
+
+
 WIDE_SCALES = [("f16u", 32, "float16"), ("f16u", 32, "bfloat16"), ("f16u", 32, "float32"), ("f16u", 128, "float16"),
                ("f16u", 512, "bfloat16")]
 

@@ -544,7 +544,9 @@ static int32_t workspace_for(cudaStream_t stream, Workspace *&out) {
   Workspace w;
   B200_CUDA_TRY(cudaMalloc((void **)&w.ws, WS_BYTES));
   B200_CUDA_TRY(cudaMalloc((void **)&w.tickets, TICKETS * sizeof(unsigned int)));
-  B200_CUDA_TRY(cudaMemset(w.tickets, 0, TICKETS * sizeof(unsigned int)));
+  // on the caller's stream, the only one that uses this workspace: ordered before its kernels
+  // even when that stream does not synchronise with the legacy default stream
+  B200_CUDA_TRY(cudaMemsetAsync(w.tickets, 0, TICKETS * sizeof(unsigned int), stream));
   w.ws_bytes = WS_BYTES;
   w.tickets_n = TICKETS;
   out = &(g_ws[{dev, stream}] = w);
