@@ -179,6 +179,26 @@ def test_e8m0_special_bytes(m):
     assert np.all(np.abs(y0 - r0) <= 1e-3 * np.maximum(np.abs(r0), 1.0))
 
 
+@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("edge", ["finite", "beyond"])
+def test_gemv_bf16_beyond_fp16(m, edge):
+    """The decode GEMV stages bf16 x as fp16: 65280 (the largest bf16 below 2^16) stays finite,
+    65536 and beyond take the power-of-two prescale; both match the oracle."""
+    from tinygrad_dx12_b200.linalg import _packed_linear
+
+    rng = np.random.default_rng(23)
+    spec = ref.make_packed(rng, "fp4_e2m1", 512, 2048, 32, "e8m0")
+    w = to_device(spec, DEV, "e8m0")
+    x = rng.standard_normal((m, 2048)).astype(np.float32)
+    x[:, 7] = 65280.0 if edge == "finite" else 65536.0
+    x[:, 900] = -65280.0 if edge == "finite" else -3.0e6
+    xt = torch.from_numpy(x).to(DEV).to(torch.bfloat16)
+    y = _packed_linear(w, xt, torch.float32, "gemv").cpu().numpy()
+    wf = ref.dequant(spec.data, spec.format, spec.shape, oracle_scales(spec, "e8m0")[0], 32, "float32",
+                     oracle_scales(spec, "e8m0")[1])
+    assert_close(y, xt.float().cpu().numpy() @ wf.T, "float32")
+
+
 @pytest.mark.parametrize("bs", [64, 128, 256, 512])
 @pytest.mark.parametrize("scale", ["float16", "bfloat16", "float32"])
 @pytest.mark.parametrize("m", [1, 2])

@@ -237,23 +237,31 @@ __device__ __forceinline__ bool stage_x_consumers(const Params &p, __half *xs, i
         const int k8 = k0 + j * NC * 32;
         if (k8 >= n8) break;
         const uint32_t wv[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
-        uint32_t h[8];
+        uint32_t hh[4];  // fp16 pairs (elements 2i, 2i+1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          if (xbf16) {
+          if (xbf16 && prescale == 1.f) {
+            // one f32x2 -> f16x2 convert per pair; |x| >= 65536 (bf16 magnitude bits >= 0x4780:
+            // the largest bf16 below, 65280, is finite in fp16) or Inf / NaN sets bit 15 of a
+            // 16-bit lane of (bits & 0x7FFF) + 0x3880, with no carry into the other lane
+            const __half2 h2 = __floats2half2_rn(__uint_as_float(wv[i] << 16), __uint_as_float(wv[i] & 0xFFFF0000u));
+            hh[i] = *reinterpret_cast<const uint32_t *>(&h2);
+            ok = ok && (((wv[i] & 0x7FFF7FFFu) + 0x38803880u) & 0x80008000u) == 0u;
+          } else if (xbf16) {
             const __half lo = __float2half_rn(__uint_as_float(wv[i] << 16) * prescale);
             const __half hi = __float2half_rn(__uint_as_float(wv[i] & 0xFFFF0000u) * prescale);
             ok = ok && !(__hisinf(lo) | __hisinf(hi));
-            h[2 * i] = __half_as_ushort(lo), h[2 * i + 1] = __half_as_ushort(hi);
+            hh[i] = (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
           } else {
-            h[2 * i] = wv[i] & 0xFFFFu, h[2 * i + 1] = wv[i] >> 16;
+            hh[i] = wv[i];
           }
         }
         uint4 o;
-        if constexpr (pairs_04<FMT>())
-          o = make_uint4(h[0] | (h[4] << 16), h[1] | (h[5] << 16), h[2] | (h[6] << 16), h[3] | (h[7] << 16));
+        if constexpr (pairs_04<FMT>())  // (e0, e4), (e1, e5), (e2, e6), (e3, e7)
+          o = make_uint4(__byte_perm(hh[0], hh[2], 0x5410), __byte_perm(hh[0], hh[2], 0x7632),
+                         __byte_perm(hh[1], hh[3], 0x5410), __byte_perm(hh[1], hh[3], 0x7632));
         else
-          o = make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
+          o = make_uint4(hh[0], hh[1], hh[2], hh[3]);
         *reinterpret_cast<uint4 *>(xs + (int64_t)mm * K + 8 * k8) = o;
       }
     }
